@@ -1,0 +1,143 @@
+/*
+ * bi.h -- C ABI of libbi.so, the batch-invariant GEMM and attention kernels for
+ * NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream
+ * handle (cudaStream_t passed as void*).  Nothing here allocates device memory, no
+ * call synchronises the stream, and no call aborts: each returns a bi_status.
+ * Work is enqueued asynchronously on `stream` and is safe to capture in a CUDA
+ * graph.
+ *
+ * The reference library (mlx-batch-invariant 0.2.0) has no C ABI of its own: its
+ * kernels are Metal source strings launched by MLX from Python.  Each entry point
+ * below replaces the Python-level operator named beside it; the Python package
+ * mlx_batch_invariant_b200 binds them with ctypes and keeps the reference's
+ * signatures, argument meaning and errors.
+ *
+ * Invariance contract: for a given (K, N, dtype, layout) the GEMM uses one tile
+ * shape and one K order whatever M is, and the attention kernel folds keys in one
+ * fixed order whatever B, H, qL are; so any output row's bits do not depend on the
+ * other rows computed with it.
+ */
+#ifndef BI_H_
+#define BI_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types.  The values are part of the ABI. */
+typedef enum {
+  BI_F32 = 0,
+  BI_F16 = 1,
+  BI_BF16 = 2
+} bi_dtype;
+
+/* Status codes: 0 on success, negative on error. */
+typedef enum {
+  BI_OK = 0,
+  BI_ERR_INVALID = -1,       /* bad shape, stride, pointer or argument          */
+  BI_ERR_UNSUPPORTED = -2,   /* valid request this build has no kernel for      */
+  BI_ERR_MISALIGNED = -3,    /* pointer or stride breaks the 16-byte rule       */
+  BI_ERR_CUDA = -4,          /* a CUDA runtime call failed (see message)        */
+  BI_ERR_TIMEOUT = -5,       /* a bounded device-side wait gave up (device flag) */
+  BI_ERR_NO_DEVICE = -6      /* no CUDA device / not an sm_100 device            */
+} bi_status;
+
+/* Routes a GEMM can take (see bi_gemm_route). */
+typedef enum {
+  BI_ROUTE_TCGEN05 = 0,      /* tcgen05/TMEM tensor-core kernel fed by TMA      */
+  BI_ROUTE_SIMT = 1          /* CUDA-core fp32 FMA kernel, sequential K         */
+} bi_route;
+
+/*
+ * out[m, n] = round_T( alpha * sum_k a[m, k] * B[k, n]  (+ beta * bias[n]) )
+ *
+ * Replaces mlx_batch_invariant/_gemm.py:_gemm (and through it matmul :225-227,
+ * addmm :230-232, linear :235-240 of the reference, whose kernel is the MSL
+ * string bi_gemm at _gemm.py:29-130).
+ *
+ *   a      (M, K) row-major, row stride lda elements.
+ *   b      b_is_nk = 1: (N, K) row-major (the nn.Linear weight layout), stride ldb.
+ *          b_is_nk = 0: (K, N) row-major, stride ldb.
+ *   bias   nullable; (N,) contiguous.  When null, alpha and beta are ignored and the
+ *          accumulator is rounded as is (reference: HAS_BIAS = 0).
+ *   out    (M, N) row-major, row stride ldo elements, same dtype as a and b.
+ *
+ * The sum is accumulated in fp32 over k in one fixed order that depends only on
+ * (K, dtype), with no split-K, no atomics; the bias is added to the fp32 value
+ * (v = alpha*acc, then v + beta*bias, each rounded to fp32) before the single
+ * rounding to the output type.  M = 0 or N = 0 is a no-op; K = 0 gives the bias
+ * term alone.
+ */
+int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb,
+            const void* bias, void* out, int64_t ldo,
+            int64_t M, int64_t N, int64_t K, int b_is_nk,
+            float alpha, float beta, int dtype, void* stream);
+
+/*
+ * The kernel route and CTA tile bi_gemm uses for (dtype, K, N, layout).  The result
+ * never depends on M; this is the library's analogue of the reference's public
+ * TILE constant (_gemm.py:172-174).  Any out-pointer may be null.
+ */
+int bi_gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk,
+                  int* route, int* bm, int* bn, int* bk);
+
+/*
+ * out[b, h, s, :] = softmax(scale * q[b, h, s, :] . k[b, kvh, i, :] + mask) . v
+ *
+ * Replaces mlx_batch_invariant/_attention.py:scaled_dot_product_attention
+ * (:205-250) and its MSL kernel bi_sdpa (:32-149).
+ *
+ *   q      (B, H, qL, D) with element strides q_strides[0..2] for b, h, s; the last
+ *          dimension contiguous.
+ *   k, v   (B, Hkv, N, D) and (B, Hkv, N, V); strides k_strides / v_strides for b
+ *          and h; each head's (N, D) block must be row-contiguous.
+ *   mask   mask_mode 0: none.  1: causal, query s sees keys i <= causal_offset + s
+ *          (the reference's bottom-right rule is causal_offset = N - qL).
+ *          2: additive mask in the q dtype, element strides mask_strides[0..2] for
+ *          (b, h, s) (0 to broadcast), last dimension contiguous; a key whose mask
+ *          value is <= -3e38 (i.e. -inf) is skipped, not added.
+ *   sinks  nullable; (H,) in the q dtype, one extra logit per query head
+ *          (reference _attention.py:80-86).
+ *   out    (B, H, qL, V) with element strides out_strides[0..2], last dim contiguous.
+ *
+ * H % Hkv == 0; D and V multiples of 32 with D == V, D <= 256.  Each (query row,
+ * head) is reduced by one CTA over all N keys in 32 fixed strides (key i folds into
+ * partial i % 32) with an fp32 online softmax and a fixed combine; there is no
+ * split-KV and no route that depends on qL, B or N.  A row with no visible key
+ * returns zeros.
+ */
+int bi_sdpa(const void* q, const int64_t q_strides[3],
+            const void* k, const int64_t k_strides[2],
+            const void* v, const int64_t v_strides[2],
+            const void* mask, const int64_t mask_strides[3], int mask_mode,
+            int64_t causal_offset, const void* sinks, float scale,
+            int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N,
+            int64_t D, int64_t V, int dtype,
+            void* out, const int64_t out_strides[3], void* stream);
+
+/* Static description of a status code. */
+const char* bi_status_string(int status);
+
+/* Detail of the last host-side error on the calling thread ("" if none). */
+const char* bi_last_error(void);
+
+/*
+ * Reads and (if clear != 0) resets the device-side error word of the current
+ * device.  Kernels set it, instead of hanging, when a bounded wait gives up.
+ * Synchronises the device.  Returns 0 when no kernel reported an error, else the
+ * code a kernel stored (site << 8 | reason).
+ */
+int bi_device_error(int clear);
+
+/* Library version as major*10000 + minor*100 + patch. */
+int bi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BI_H_ */

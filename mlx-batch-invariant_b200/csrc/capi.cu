@@ -1,0 +1,236 @@
+// extern "C" entry points of libbi.so (declared in include/bi.h): argument
+// validation, route selection and error reporting.  The kernels live in
+// gemm_tcgen05.cu, gemm_simt.cu and sdpa.cu.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <atomic>
+
+#include "internal.h"
+
+namespace bi {
+
+static thread_local char g_msg[512] = "";
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return BI_OK;
+  return set_error(BI_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+std::atomic<int> g_cc_major[kMaxDevices];
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int elem_size(int dtype) { return dtype == BI_F32 ? 4 : 2; }
+}  // namespace
+
+int device_sm_count() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  int v = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
+      v = 148;
+    }
+    g_sm_count[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+int device_cc_major() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  int v = g_cc_major[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+      return -1;
+    }
+    g_cc_major[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+// The GEMM route for (dtype, K, N, layout).  Never a function of M.
+static int gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk) {
+  if (dtype == BI_F32) return BI_ROUTE_SIMT;
+  if (K <= 0 || K % 8 != 0) return BI_ROUTE_SIMT;
+  if (!b_is_nk && N % 8 != 0) return BI_ROUTE_SIMT;
+  return BI_ROUTE_TCGEN05;
+}
+
+static int check_device() {
+  const int cc = device_cc_major();
+  if (cc < 0) return set_error(BI_ERR_NO_DEVICE, "no CUDA device is current");
+  if (cc != 10) {
+    return set_error(BI_ERR_NO_DEVICE, "libbi.so is built for sm_100a; current device is sm_%d*",
+                     cc);
+  }
+  return BI_OK;
+}
+
+}  // namespace bi
+
+using namespace bi;
+
+extern "C" {
+
+int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias, void* out,
+            int64_t ldo, int64_t M, int64_t N, int64_t K, int b_is_nk, float alpha, float beta,
+            int dtype, void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
+  }
+  if (M < 0 || N < 0 || K < 0) return set_error(BI_ERR_INVALID, "negative dimension");
+  if (M == 0 || N == 0) return BI_OK;
+  if (out == nullptr) return set_error(BI_ERR_INVALID, "out is null");
+  if (K > 0 && (a == nullptr || b == nullptr)) return set_error(BI_ERR_INVALID, "a or b is null");
+  if (lda < K || ldo < N || ldb < (b_is_nk ? K : N)) {
+    return set_error(BI_ERR_INVALID, "leading dimension smaller than the row");
+  }
+  int st = check_device();
+  if (st) return st;
+
+  GemmArgs g{a, lda, b, ldb, bias, out, ldo, M, N, K, b_is_nk ? 1 : 0, alpha, beta, dtype};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (gemm_route(dtype, K, N, b_is_nk) == BI_ROUTE_TCGEN05) {
+    if (!aligned16(a) || !aligned16(b) || lda % 8 != 0 || ldb % 8 != 0) {
+      return set_error(BI_ERR_MISALIGNED,
+                       "tensor-core route needs 16-byte aligned a/b and row strides that are "
+                       "multiples of 8 elements");
+    }
+    return launch_gemm_tc(g, s);
+  }
+  return launch_gemm_simt(g, s);
+}
+
+int bi_gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk, int* route, int* bm, int* bn,
+                  int* bk) {
+  if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
+  }
+  const int r = gemm_route(dtype, K, N, b_is_nk);
+  if (route) *route = r;
+  if (bm) *bm = r == BI_ROUTE_TCGEN05 ? kTcBM : kSimtBM;
+  if (bn) *bn = r == BI_ROUTE_TCGEN05 ? kTcBN : kSimtBN;
+  if (bk) *bk = r == BI_ROUTE_TCGEN05 ? kTcBK : kSimtBK;
+  return BI_OK;
+}
+
+int bi_sdpa(const void* q, const int64_t q_strides[3], const void* k, const int64_t k_strides[2],
+            const void* v, const int64_t v_strides[2], const void* mask,
+            const int64_t mask_strides[3], int mask_mode, int64_t causal_offset,
+            const void* sinks, float scale, int64_t B, int64_t H, int64_t Hkv, int64_t qL,
+            int64_t N, int64_t D, int64_t V, int dtype, void* out, const int64_t out_strides[3],
+            void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
+  }
+  if (B < 0 || H < 0 || Hkv < 0 || qL < 0 || N < 0 || D <= 0 || V <= 0) {
+    return set_error(BI_ERR_INVALID, "negative or empty dimension");
+  }
+  if (Hkv == 0 || H % Hkv != 0) return set_error(BI_ERR_INVALID, "H must be a multiple of Hkv");
+  if (D % 32 != 0 || V % 32 != 0) {
+    return set_error(BI_ERR_INVALID, "head dimensions must be multiples of 32");
+  }
+  if (D != V || D > 256) {
+    return set_error(BI_ERR_UNSUPPORTED, "built for D == V <= 256 (got D=%lld V=%lld)",
+                     static_cast<long long>(D), static_cast<long long>(V));
+  }
+  if (mask_mode < 0 || mask_mode > 2) return set_error(BI_ERR_INVALID, "mask_mode must be 0..2");
+  if (B == 0 || H == 0 || qL == 0) return BI_OK;
+  if (!q_strides || !k_strides || !v_strides || !out_strides) {
+    return set_error(BI_ERR_INVALID, "stride array is null");
+  }
+  if (mask_mode == 2 && (mask == nullptr || mask_strides == nullptr)) {
+    return set_error(BI_ERR_INVALID, "mask_mode 2 needs a mask and its strides");
+  }
+  if (B > INT32_MAX || H > INT32_MAX || qL > INT32_MAX || N > INT32_MAX) {
+    return set_error(BI_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
+  }
+  if (q == nullptr || out == nullptr || (N > 0 && (k == nullptr || v == nullptr))) {
+    return set_error(BI_ERR_INVALID, "q, k, v or out is null");
+  }
+  const int64_t vec = 16 / elem_size(dtype);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || q_strides[0] % vec ||
+      q_strides[1] % vec || q_strides[2] % vec || k_strides[0] % vec || k_strides[1] % vec ||
+      v_strides[0] % vec || v_strides[1] % vec) {
+    return set_error(BI_ERR_MISALIGNED,
+                     "q, k, v must be 16-byte aligned with strides that are multiples of 16 bytes");
+  }
+  int st = check_device();
+  if (st) return st;
+
+  SdpaArgs a;
+  a.q = q;
+  for (int i = 0; i < 3; ++i) a.qs[i] = q_strides[i];
+  a.k = k;
+  a.ks[0] = k_strides[0];
+  a.ks[1] = k_strides[1];
+  a.v = v;
+  a.vs[0] = v_strides[0];
+  a.vs[1] = v_strides[1];
+  a.mask = mask_mode == 2 ? mask : nullptr;
+  for (int i = 0; i < 3; ++i) a.ms[i] = mask_mode == 2 ? mask_strides[i] : 0;
+  a.mask_mode = mask_mode;
+  a.causal_offset = causal_offset;
+  a.sinks = sinks;
+  a.scale = scale;
+  a.B = B;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.qL = qL;
+  a.N = N;
+  a.D = D;
+  a.V = V;
+  a.dtype = dtype;
+  a.out = out;
+  for (int i = 0; i < 3; ++i) a.os[i] = out_strides[i];
+  return launch_sdpa(a, static_cast<cudaStream_t>(stream));
+}
+
+const char* bi_status_string(int status) {
+  switch (status) {
+    case BI_OK: return "ok";
+    case BI_ERR_INVALID: return "invalid argument";
+    case BI_ERR_UNSUPPORTED: return "unsupported";
+    case BI_ERR_MISALIGNED: return "misaligned pointer or stride";
+    case BI_ERR_CUDA: return "CUDA error";
+    case BI_ERR_TIMEOUT: return "device wait timed out";
+    case BI_ERR_NO_DEVICE: return "no suitable CUDA device";
+    default: return "unknown status";
+  }
+}
+
+const char* bi_last_error(void) { return g_msg; }
+
+int bi_device_error(int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
+  unsigned w = read_error_gemm_tc(clear != 0);
+  const unsigned s = read_error_sdpa(clear != 0);
+  if (w == 0 && s != 0) w = s | (1u << 16);  // sdpa sites are tagged in bit 16
+  return static_cast<int>(w);
+}
+
+int bi_version(void) { return 100; }  // 0.1.0
+
+}  // extern "C"

@@ -1,0 +1,419 @@
+// Batch-invariant GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), fed by
+// TMA, for fp16 and bf16 inputs with fp32 accumulation.
+//
+// Invariance argument (the property mlx_batch_invariant/_gemm.py:1-24 states for
+// its Metal kernel): every output element is produced by one CTA that owns the
+// whole K reduction.  The CTA tile (128 x 256), the K block (64) and the UMMA
+// instruction (M=128, N=256, K=16) are compile-time constants, so element (m, n)
+// is always accumulated as the same sequence of K=16 tensor-core steps, k
+// ascending, into an fp32 TMEM accumulator -- for every M, every row position in
+// the tile and every column shard.  There is no split-K, no stream-K and no
+// atomic.  Which CTA takes which tile (the persistent schedule below) changes with
+// M; the arithmetic per element does not.
+//
+// Structure: one persistent CTA per SM, 6 warps.
+//   warp 0      TMA producer: A (M x K, K-major) and B tiles into a 4-stage ring.
+//   warp 1      TMEM allocator and UMMA issuer (one thread), two accumulator
+//               buffers of 256 fp32 columns so the epilogue of tile i overlaps the
+//               main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, alpha/bias in fp32, one
+//               rounding to the output type, vector stores.
+// Every mbarrier wait is bounded; a wait that gives up raises the device error word
+// and the CTA drains its own in-flight copies and MMAs, frees TMEM and exits.
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace bi {
+namespace tc {
+
+constexpr int BM = kTcBM;
+constexpr int BN = kTcBN;
+constexpr int BK = kTcBK;  // 64 x 2 bytes = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int UMMA_K = 16;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int ACC_BUFS = 2;
+constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512: the whole tensor memory of the SM
+constexpr int NUM_THREADS = 192;
+constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
+constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES + NUM_BARRIERS * 8 + 16;
+constexpr int GROUP_M = 16;  // tiles of M that consecutive tile indices sweep (L2 reuse)
+
+// Error sites (code = site << 8 | reason).
+enum : unsigned { kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4 };
+
+__device__ unsigned g_error_word = 0;
+
+struct Params {
+  const void* bias;
+  void* out;
+  int64_t ldo;
+  int M, N, K;
+  float alpha, beta;
+  int has_bias;
+  int tiles_m, tiles_n, num_tiles;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = GROUP_M * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int rows = min(tiles_m - first_m, GROUP_M);
+  const int in_group = tile - group * per_group;
+  tm = first_m + in_group % rows;
+  tn = in_group / rows;
+}
+
+template <typename T, bool B_NK>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + ACC_BUFS;
+  uint64_t* mma_done = bars + 2 * STAGES + 2 * ACC_BUFS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARRIERS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < ACC_BUFS; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      // Parity of the most recent fill of each stage, for the drain on abort.
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sA + stage * A_STAGE_BYTES, &tmap_a, &full[stage], kb * BK, tm * BM);
+          uint8_t* dstB = sB + stage * B_STAGE_BYTES;
+          if (B_NK) {
+            tma_load_2d(dstB, &tmap_b, &full[stage], kb * BK, tn * BN);
+          } else {
+            // (K, N) row-major B: four 64-column slabs, each 64 k-rows of 128 bytes.
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              tma_load_2d(dstB + j * (64 * BK * 2), &tmap_b, &full[stage], tn * BN + j * 64,
+                          kb * BK);
+            }
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (kSiteProducer << 8) | kErrReasonTimeout);
+        // Drain: wait (bounded) for every fill this thread started.
+        for (int s = 0; s < STAGES; ++s) {
+          if (issued_mask & (1u << s)) {
+            if (!mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr)) {
+              record_error(&g_error_word, (kSiteDrain << 8) | kErrReasonTimeout);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- UMMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t fmt = (dtype_of<T>::value == 2) ? 1u : 0u;
+      constexpr uint32_t idesc = umma_idesc_f16(fmt, B_NK ? 0u : 1u, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart;
+            // the K=16 step moves 32 bytes along the row.
+            const uint64_t adesc = umma_smem_desc(a_base + k * UMMA_K * 2, 16, 1024, 2);
+            uint64_t bdesc;
+            if (B_NK) {
+              bdesc = umma_smem_desc(b_base + k * UMMA_K * 2, 16, 1024, 2);
+            } else {
+              // MN-major, 128-byte swizzle: 64-column slabs 8 KiB apart (LBO), 8-k-row
+              // groups 1024 B apart (SBO); the K=16 step moves 16 rows = 2048 B.
+              bdesc = umma_smem_desc(b_base + k * UMMA_K * 128, 64 * BK * 2, 1024, 2);
+            }
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);  // accumulator ready for the epilogue
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (kSiteMma << 8) | kErrReasonTimeout);
+      }
+      // Whatever happened, wait until every MMA this thread issued has finished
+      // before the CTA releases TMEM and shared memory.
+      umma_commit(mma_done);
+      if (!mbar_wait(mma_done, 0, nullptr)) {
+        record_error(&g_error_word, (kSiteDrain << 8) | kErrReasonTimeout);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter..+31
+    const int row_in_tile = quarter * 32 + lane;
+    const T* bias = static_cast<const T*>(p.bias);
+    T* out = static_cast<T*>(p.out);
+    const bool vec_ok = (p.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      bool ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) {
+          *abort_flag = 1;
+          record_error(&g_error_word, (kSiteEpilogue << 8) | kErrReasonTimeout);
+        }
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+      const bool row_ok = row < p.M;
+      T* orow = out + row * p.ldo;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld_32x32b_x32(tmem_base + buf * BN + c + (static_cast<uint32_t>(quarter * 32) << 16),
+                           r);
+        tmem_ld_wait();
+        const int col0 = tn * BN + c;
+        if (!row_ok || col0 >= p.N) continue;
+        if (vec_ok && col0 + 32 <= p.N) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float b0 = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
+            const float b1 = p.has_bias ? to_f32(bias[col0 + j + 1]) : 0.f;
+            const T lo = gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, b0);
+            const T hi =
+                gemm_epilogue<T>(__uint_as_float(r[j + 1]), p.has_bias, p.alpha, p.beta, b1);
+            packed[j / 2] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                            (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                                packed[4 * q + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              const float bj = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
+              orow[col0 + j] =
+                  gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, bj);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 2-D tensor map over a row-major (rows, cols) matrix of 16-bit elements with the
+// given row stride (elements), box (box_cols x box_rows), 128-byte swizzle, and
+// zero fill outside the matrix.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                    int64_t row_stride, uint32_t box_cols, uint32_t box_rows, int dtype) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(BI_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const CUtensorMapDataType dt =
+      dtype == BI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return set_error(BI_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld",
+                     static_cast<int>(r), static_cast<long long>(rows),
+                     static_cast<long long>(cols));
+  }
+  return BI_OK;
+}
+
+template <typename T, bool B_NK>
+static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, BM, g.dtype);
+  if (st) return st;
+  if (B_NK) {
+    st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, BN, g.dtype);
+  } else {
+    st = make_map(&mb, g.b, g.K, g.N, g.ldb, 64, BK, g.dtype);
+  }
+  if (st) return st;
+
+  auto kern = gemm_tc_kernel<T, B_NK>;
+  // The attribute is per device; setting it again is cheap and capture-safe.
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_tc)");
+
+  Params p;
+  p.bias = g.bias;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  p.M = static_cast<int>(g.M);
+  p.N = static_cast<int>(g.N);
+  p.K = static_cast<int>(g.K);
+  p.alpha = g.alpha;
+  p.beta = g.beta;
+  p.has_bias = g.bias != nullptr;
+  p.tiles_m = static_cast<int>((g.M + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((g.N + BN - 1) / BN);
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  const int grid = p.num_tiles < device_sm_count() ? p.num_tiles : device_sm_count();
+  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  return cuda_status(cudaGetLastError(), "gemm_tc launch");
+}
+
+}  // namespace tc
+
+int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) {
+    return set_error(BI_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
+  }
+  if (g.dtype == BI_BF16) {
+    return g.b_is_nk ? tc::launch_typed<__nv_bfloat16, true>(g, stream)
+                     : tc::launch_typed<__nv_bfloat16, false>(g, stream);
+  }
+  if (g.dtype == BI_F16) {
+    return g.b_is_nk ? tc::launch_typed<__half, true>(g, stream)
+                     : tc::launch_typed<__half, false>(g, stream);
+  }
+  return set_error(BI_ERR_UNSUPPORTED, "tensor-core route takes fp16 or bf16");
+}
+
+unsigned read_error_gemm_tc(bool clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, tc::g_error_word, sizeof(v));
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(tc::g_error_word, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace bi
