@@ -1,10 +1,12 @@
 """GPU parity and invariance tests of the batch-invariant GEMM (libbi.so bi_gemm).
 
-Parity bar: float32 (CUDA-core route, sequential-K fmaf) is bit-exact against the
-host oracle; float16 / bfloat16 on the tensor-core route are within 1 ulp of the
-oracle's sequential-K fp32 emulation after rounding, except where the exact sum
-nearly cancels (|oracle| below 2^-10 of the row's largest output), where the bound
-is 2 ulp of that row scale.  Invariance bar: 0 differing bits.
+Parity bar: float32 (CUDA-core route) and float16 / bfloat16 shapes on the CUDA-core
+route are bit-exact against the host oracle (same K order).  float16 / bfloat16 on
+the tensor-core route accumulate the same K products in fp32 in another order (K=16
+hardware steps), so they must be within 1 ulp of the oracle's emulation after
+rounding plus the fp32 reordering allowance 2^-21 * sum_k |a[m,k] * b[k,n]| -- the
+allowance only matters where the sum nearly cancels and an output-type ulp is finer
+than fp32 accumulation noise.  Invariance bar: 0 differing bits.
 """
 
 import numpy as np
@@ -26,21 +28,24 @@ def bi():
     return bi
 
 
-def _ulp_ok(got, want, dtype):
-    """Tensor-core tolerance stated in the module docstring."""
-    g = to_np(got).astype(np.float64)
-    w = to_np(want).astype(np.float64)
+def _ulp_ok(got, want, dtype, absterm=None):
+    """Tolerance stated in the module docstring; absterm = |a| @ |b| (float64)."""
     if dtype == torch.float32:
         return np.array_equal(bits(got), bits(torch.from_numpy(to_np(want).copy())))
-    # ulp of each oracle value (spacing of the format at |w|)
+    g = to_np(got).astype(np.float64)
+    w = to_np(want).astype(np.float64)
     u = UNIT[dtype]
-    mag = np.maximum(np.abs(w), np.finfo(np.float32).tiny)
+    mag = np.maximum(np.abs(w), 2.0 ** -24)
     ulp = 2.0 ** np.floor(np.log2(mag)) * u
-    rowscale = np.abs(w).max(axis=-1, keepdims=True)
-    floor_ulp = 2.0 ** np.floor(np.log2(np.maximum(rowscale, 1e-30))) * u
-    tol = np.where(np.abs(w) < rowscale * 2.0 ** -10, 2 * floor_ulp, ulp)
+    tol = ulp + (2.0 ** -21 * absterm if absterm is not None else 0.0)
     bad = np.abs(g - w) > tol * (1 + 1e-9)
     return not bad.any()
+
+
+def _absterm(x, w, b_is_nk):
+    a = np.abs(to_np(x).astype(np.float64))
+    b = np.abs(to_np(w).astype(np.float64))
+    return a @ (b.T if b_is_nk else b)
 
 
 def _case(bi, dtype, M, K, N, b_is_nk, with_bias, alpha=1.0, beta=1.0, seed=0):
@@ -56,7 +61,8 @@ def _case(bi, dtype, M, K, N, b_is_nk, with_bias, alpha=1.0, beta=1.0, seed=0):
         y = bi.matmul(x, w)
     want = orc.gemm(to_np(x), to_np(w), to_np(bias) if with_bias else None, b_is_nk=b_is_nk,
                     alpha=alpha, beta=beta)
-    return y, torch.from_numpy(want.view(np.uint16) if dtype == torch.bfloat16 else want)
+    absterm = abs(alpha) * _absterm(x, w, b_is_nk)
+    return y, torch.from_numpy(want.view(np.uint16) if dtype == torch.bfloat16 else want), absterm
 
 
 SHAPES = [(1, 64, 8), (3, 72, 100), (7, 128, 256), (130, 264, 300), (129, 1000, 520),
@@ -68,19 +74,19 @@ SHAPES = [(1, 64, 8), (3, 72, 100), (7, 128, 256), (130, 264, 300), (129, 1000, 
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_parity_against_oracle(bi, dtype, b_is_nk, with_bias):
     for (M, K, N) in SHAPES:
-        y, want = _case(bi, dtype, M, K, N, b_is_nk, with_bias, seed=M + K)
+        y, want, absterm = _case(bi, dtype, M, K, N, b_is_nk, with_bias, seed=M + K)
         if dtype == torch.bfloat16:
             want = want.view(torch.bfloat16)
-        assert _ulp_ok(y, want, dtype), "%s M=%d K=%d N=%d nk=%d bias=%d" % (
+        assert _ulp_ok(y, want, dtype, absterm), "%s M=%d K=%d N=%d nk=%d bias=%d" % (
             dtype, M, K, N, b_is_nk, with_bias)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_alpha_beta_epilogue(bi, dtype):
-    y, want = _case(bi, dtype, 33, 256, 264, False, True, alpha=0.5, beta=-2.0, seed=9)
+    y, want, absterm = _case(bi, dtype, 33, 256, 264, False, True, alpha=0.5, beta=-2.0, seed=9)
     if dtype == torch.bfloat16:
         want = want.view(torch.bfloat16)
-    assert _ulp_ok(y, want, dtype)
+    assert _ulp_ok(y, want, dtype, absterm)
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
@@ -88,7 +94,7 @@ def test_unaligned_k_takes_cuda_core_route_bit_exact(bi, dtype):
     """K % 8 != 0 cannot feed TMA; the CUDA-core route is the oracle's exact order."""
     assert bi.tile_for(dtype, 1001, 64, True)["route"] == "simt"
     for b_is_nk in (True, False):
-        y, want = _case(bi, dtype, 9, 1001, 70, b_is_nk, True, seed=3)
+        y, want, _ = _case(bi, dtype, 9, 1001, 70, b_is_nk, True, seed=3)
         assert np.array_equal(bits(y), want.numpy().reshape(-1).view(
             np.uint16 if dtype != torch.float32 else np.uint32))
 
