@@ -59,9 +59,10 @@ def gather_columns(y_local, n_total, group=None):
         pad = torch.zeros((M, per), dtype=y.dtype, device=y.device)
         pad[:, :y.shape[1]] = y
         y = pad
-    gathered = torch.empty((world, M, per), dtype=y.dtype, device=y.device)
+    # rank blocks concatenated along dim 0 (the layout every backend accepts)
+    gathered = torch.empty((world * M, per), dtype=y.dtype, device=y.device)
     dist.all_gather_into_tensor(gathered, y.contiguous(), group=group)
-    out = gathered.permute(1, 0, 2).reshape(M, world * per)
+    out = gathered.view(world, M, per).permute(1, 0, 2).reshape(M, world * per)
     if world * per != n_total:
         out = out[:, :n_total]
     return out.contiguous()
@@ -90,10 +91,10 @@ def gather_heads(y_local, group=None):
     if world == 1:
         return y_local
     B, hl, qL, V = y_local.shape
-    gathered = torch.empty((world,) + tuple(y_local.shape), dtype=y_local.dtype,
-                           device=y_local.device)
+    gathered = torch.empty((world * B, hl, qL, V), dtype=y_local.dtype, device=y_local.device)
     dist.all_gather_into_tensor(gathered, y_local.contiguous(), group=group)
-    return gathered.permute(1, 0, 2, 3, 4).reshape(B, world * hl, qL, V).contiguous()
+    return gathered.view(world, B, hl, qL, V).permute(1, 0, 2, 3, 4).reshape(
+        B, world * hl, qL, V).contiguous()
 
 
 def head_shard(H, Hkv, rank, world):
