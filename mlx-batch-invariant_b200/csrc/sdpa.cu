@@ -12,14 +12,20 @@
 //
 // B200 mapping:
 //   * K and V rows of the KV head are streamed through a ring of shared-memory
-//     stages with 1-D bulk copies (cp.async.bulk, mbarrier completion), 32 keys per
-//     stage -- one key per partial -- so the bytes in flight do not depend on
-//     registers.
-//   * A partial is LP consecutive threads; each holds D/LP elements of q, k, v and o
-//     (16-byte vectors where the row allows).  The q.k dot product is a sequential
-//     fmaf over the thread's elements followed by a fixed xor-butterfly over the LP
-//     threads, which leaves the identical sum in every thread of the partial.
-//   * Online-softmax update per visible key (i = key, h = head):
+//     stages with 1-D bulk copies (cp.async.bulk, one mbarrier per stage), ROWS keys
+//     per partial per stage, so the bytes in flight do not depend on registers; the
+//     last warp to finish a stage refills it, so no CTA-wide barrier sits in the loop.
+//   * A partial is LP consecutive threads, each holding E = D/LP elements of q, k, v
+//     and o (32 bytes of a key row per thread, as interleaved 16-byte vectors so a
+//     quarter warp reads distinct banks); LP is a function of (D, dtype) only.
+//   * Arithmetic uses Blackwell's packed fp32x2 FMA/MUL (fma.rn.f32x2), which rounds
+//     each lane exactly like fmaf.  The q.k dot product of a thread runs four fp32
+//     chains (its k-th element goes to chain (k/2 % 2)*2 + k%2), summed as
+//     (c0 + c1) + (c2 + c3); a fixed
+//     xor-butterfly over the LP threads sums it.  The CTA's heads share one butterfly
+//     (reduce_heads): each thread ends with one head's score and runs that head's
+//     scalar softmax step; the weights reach the other threads by shuffle.
+//   * Online-softmax update per visible key (h = head):
 //         m' = max(m, score);  f = exp(m - m');  e = exp(score - m')
 //         l  = fmaf(l, f, e);  o[j] = fmaf(e, v[j], o[j] * f);  m = m'
 //     When m' == m the multiply by f = exp(0) = 1 is skipped (bit-identical).
@@ -32,6 +38,16 @@ namespace bi {
 namespace sdpa {
 
 constexpr int PARTIALS = 32;  // also the key stride of the walk (reference BN = 32)
+
+// Key rows per partial in one shared-memory stage (stage = PARTIALS * ROWS keys), at
+// most this many; it changes how keys are staged, never the fold.
+#ifndef BI_SDPA_ROWS_PER_STAGE
+#define BI_SDPA_ROWS_PER_STAGE 2
+#endif
+// Registers per thread available for the q and o slices of the CTA's heads.
+#ifndef BI_SDPA_REG_BUDGET
+#define BI_SDPA_REG_BUDGET 64
+#endif
 
 __device__ unsigned g_error_word = 0;
 
@@ -53,52 +69,167 @@ struct Params {
   int64_t os0, os1, os2;
 };
 
-// Loads E contiguous elements of type T starting at `src` (aligned to the largest
-// power-of-two divisor of E*sizeof(T), at most 16 bytes) and widens them to fp32.
+// ---- packed fp32x2 arithmetic (each lane rounded as the scalar op) ----
+struct f2 {
+  uint64_t r;
+};
+__device__ __forceinline__ f2 pack2(float lo, float hi) {
+  return f2{static_cast<uint64_t>(__float_as_uint(lo)) |
+            (static_cast<uint64_t>(__float_as_uint(hi)) << 32)};
+}
+__device__ __forceinline__ float lo_of(f2 a) { return __uint_as_float(static_cast<uint32_t>(a.r)); }
+__device__ __forceinline__ float hi_of(f2 a) {
+  return __uint_as_float(static_cast<uint32_t>(a.r >> 32));
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+
+// A thread's share of a D-element row: E elements taken as NV vectors of W bytes
+// (W = 16, 8 or 4, whichever divides E*sizeof(T)), vector c of thread `sub` starting
+// at element (c*LP + sub)*PER.  Interleaving the threads' vectors keeps each quarter
+// warp's shared-memory reads on distinct banks.
 template <typename T, int E>
-__device__ __forceinline__ void load_vec(const T* src, float (&dst)[E]) {
-  constexpr int BYTES = E * static_cast<int>(sizeof(T));
-  constexpr int W = (BYTES % 16 == 0) ? 16 : (BYTES % 8 == 0) ? 8 : (BYTES % 4 == 0) ? 4 : 2;
-  constexpr int PER = W / static_cast<int>(sizeof(T)) > 0 ? W / static_cast<int>(sizeof(T)) : 1;
-  if constexpr (W >= static_cast<int>(sizeof(T))) {
+struct RowSlice {
+  static constexpr int BYTES = E * static_cast<int>(sizeof(T));
+  static constexpr int W = (BYTES % 16 == 0) ? 16 : (BYTES % 8 == 0) ? 8 : 4;
+  static constexpr int PER = W / static_cast<int>(sizeof(T));  // elements per vector
+  static constexpr int NV = E / PER;                           // vectors per thread
+  static constexpr int WORDS = W / 4;
+};
+
+// Element index (within the row) of the thread's k-th element.
+template <typename T, int E, int LP>
+__device__ __forceinline__ int slice_elem(int sub, int k) {
+  using RS = RowSlice<T, E>;
+  return ((k / RS::PER) * LP + sub) * RS::PER + k % RS::PER;
+}
+
+// Loads the thread's slice of a row (see RowSlice) and widens it to E/2 packed fp32
+// pairs (the thread's element 2j in the low half, 2j+1 in the high half).
+template <typename T, int E, int LP>
+__device__ __forceinline__ void load_slice(const T* row, int sub, f2 (&dst)[E / 2]) {
+  using RS = RowSlice<T, E>;
+  constexpr int WORDS = RS::WORDS;
 #pragma unroll
-    for (int c = 0; c < E / PER; ++c) {
-      T tmp[PER];
-      if constexpr (W == 16) {
-        *reinterpret_cast<uint4*>(tmp) = *reinterpret_cast<const uint4*>(src + c * PER);
-      } else if constexpr (W == 8) {
-        *reinterpret_cast<uint2*>(tmp) = *reinterpret_cast<const uint2*>(src + c * PER);
-      } else if constexpr (W == 4) {
-        *reinterpret_cast<uint32_t*>(tmp) = *reinterpret_cast<const uint32_t*>(src + c * PER);
+  for (int c = 0; c < RS::NV; ++c) {
+    const uint32_t* s =
+        reinterpret_cast<const uint32_t*>(row + (c * LP + sub) * RS::PER);
+    uint32_t w[WORDS];
+    if constexpr (RS::W == 16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(s);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    } else if constexpr (RS::W == 8) {
+      const uint2 u = *reinterpret_cast<const uint2*>(s);
+      w[0] = u.x; w[1] = u.y;
+    } else {
+      w[0] = s[0];
+    }
+#pragma unroll
+    for (int i = 0; i < WORDS; ++i) {
+      if constexpr (sizeof(T) == 4) {
+        // fp32: two words make one pair
+        if (i % 2 == 1) dst[(c * WORDS + i) / 2] = f2{static_cast<uint64_t>(w[i - 1]) |
+                                                      (static_cast<uint64_t>(w[i]) << 32)};
+      } else if constexpr (dtype_of<T>::value == 2) {
+        // bf16 pair in one word: widening is a shift / mask
+        dst[c * WORDS + i] = f2{static_cast<uint64_t>(w[i] << 16) |
+                                (static_cast<uint64_t>(w[i] & 0xffff0000u) << 32)};
       } else {
-        tmp[0] = src[c * PER];
+        const float2 fl = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        dst[c * WORDS + i] = pack2(fl.x, fl.y);
       }
-#pragma unroll
-      for (int u = 0; u < PER; ++u) dst[c * PER + u] = to_f32(tmp[u]);
     }
   }
 }
 
-template <typename T, int D, int LP, int HG, int STAGES>
-__global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
+// Head whose score thread `sub` holds after the transposed butterfly below.
+template <int LP, int HG>
+__device__ __forceinline__ int own_head(int sub) {
+  int h = 0, nv = HG;
+#pragma unroll
+  for (int off = LP / 2; off >= 1; off >>= 1) {
+    if (nv > 1) {
+      nv >>= 1;
+      if (sub & off) h += nv;
+    }
+  }
+  return h;
+}
+
+// Sums each head's per-thread partial dot over the LP threads of a partial with the
+// xor-butterfly (offsets LP/2, ..., 1).  While more than one head is in flight, each
+// level halves the heads a thread carries (the partner of a pair keeps the other
+// half), so the sum of every head is formed by exactly the additions of a plain
+// butterfly for that head -- a+b and b+a being the same fp32 value -- and thread
+// `sub` ends with the total of head own_head(sub).
+template <int LP, int HG>
+__device__ __forceinline__ float reduce_heads(float (&v)[HG], int sub) {
+  int nv = HG;
+#pragma unroll
+  for (int off = LP / 2; off >= 1; off >>= 1) {
+    if (nv > 1) {
+      const int half = nv >> 1;
+      const bool upper = (sub & off) != 0;
+#pragma unroll
+      for (int j = 0; j < HG / 2; ++j) {
+        if (j < half) {
+          const float send = upper ? v[j] : v[j + half];
+          const float keep = upper ? v[j + half] : v[j];
+          v[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+        }
+      }
+      nv = half;
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], off));
+    }
+  }
+  return v[0];
+}
+
+#ifndef BI_SDPA_MIN_BLOCKS
+#define BI_SDPA_MIN_BLOCKS 1
+#endif
+
+template <typename T, int D, int LP, int HG, int STAGES, int ROWS>
+__global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA_MIN_BLOCKS : 1))
+    sdpa_kernel(const Params p) {
   constexpr int NT = PARTIALS * LP;
+  constexpr int NW = NT / 32;  // warps
   constexpr int E = D / LP;  // elements of q/k/v/o per thread
+  constexpr int E2 = E / 2;
   constexpr int ROW_BYTES = D * static_cast<int>(sizeof(T));
-  constexpr int STAGE_ELEMS = PARTIALS * D;
-  static_assert(D % LP == 0, "D must split evenly over the partial's threads");
+  constexpr int KEYS = PARTIALS * ROWS;  // keys per stage
+  constexpr int STAGE_ELEMS = KEYS * D;
+  static_assert(D % LP == 0 && E % 2 == 0, "D must split evenly into pairs per thread");
   static_assert(32 % LP == 0, "a partial must not straddle warps");
+  static_assert(HG <= LP, "each head's softmax state needs a thread of its own");
 
   extern __shared__ __align__(128) uint8_t smem[];
   T* sK = reinterpret_cast<T*>(smem);
   T* sV = sK + STAGES * STAGE_ELEMS;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * STAGES * PARTIALS * ROW_BYTES);
-  float* comb_m = reinterpret_cast<float*>(full + STAGES);  // [PARTIALS]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * STAGES * KEYS * ROW_BYTES);
+  int* done_count = reinterpret_cast<int*>(full + STAGES);          // [STAGES]
+  int* issued_count = done_count + STAGES;
+  volatile int* abort_flag = issued_count + 1;
+  float* comb_m = reinterpret_cast<float*>(done_count + STAGES + 4);  // [PARTIALS]
   float* comb_l = comb_m + PARTIALS;                         // [PARTIALS]
   float* comb_o = reinterpret_cast<float*>(smem);            // [PARTIALS][D], after the walk
 
   const int tid = threadIdx.x;
-  const int part = tid / LP;
+  const int warp = tid >> 5;
+  const int part = tid / LP;  // meaningful for consumer threads (warp < NW)
   const int sub = tid % LP;
+  const int lane = tid & 31;
+  const int part_lane0 = lane & ~(LP - 1);  // first lane of this partial in the warp
+  const int my_head = own_head<LP, HG>(sub);
 
   // Block -> (b, head group, s); s fastest.
   const int groups = p.H / HG;
@@ -115,7 +246,7 @@ __global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
     const int64_t last = p.causal_offset + s;  // last visible key
     kmax = last < 0 ? 0 : (last + 1 < p.N ? last + 1 : p.N);
   }
-  const int nblocks = static_cast<int>((kmax + PARTIALS - 1) / PARTIALS);
+  const int nblocks = static_cast<int>((kmax + KEYS - 1) / KEYS);
 
   const T* Q = static_cast<const T*>(p.q);
   const T* Kb = static_cast<const T*>(p.k) + static_cast<int64_t>(b) * p.ks0 +
@@ -123,113 +254,160 @@ __global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
   const T* Vb = static_cast<const T*>(p.v) + static_cast<int64_t>(b) * p.vs0 +
                 static_cast<int64_t>(kvh) * p.vs1;
   const T* Mk = static_cast<const T*>(p.mask);
+  const T* mrow = Mk == nullptr ? nullptr
+                                : Mk + static_cast<int64_t>(b) * p.ms0 +
+                                      static_cast<int64_t>(h0 + my_head) * p.ms1 +
+                                      static_cast<int64_t>(s) * p.ms2;
   const T* Sk = static_cast<const T*>(p.sinks);
 
-  float qv[HG][E], o[HG][E], m[HG], l[HG];
+  f2 qv[HG][E2], o[HG][E2];
 #pragma unroll
   for (int h = 0; h < HG; ++h) {
     const T* qrow = Q + static_cast<int64_t>(b) * p.qs0 + static_cast<int64_t>(h0 + h) * p.qs1 +
-                    static_cast<int64_t>(s) * p.qs2 + sub * E;
-    float tmp[E];
-    load_vec<T, E>(qrow, tmp);
+                    static_cast<int64_t>(s) * p.qs2;
+    f2 tmp[E2];
+    load_slice<T, E, LP>(qrow, sub, tmp);
+    const f2 sc = pack2(p.scale, p.scale);
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      qv[h][e] = __fmul_rn(p.scale, tmp[e]);
-      o[h][e] = 0.f;
-    }
-    // Lowest finite float, not -inf, so a fully masked partial stays NaN-free.
-    m[h] = -3.40282347e+38f;
-    l[h] = 0.f;
-    if (Sk != nullptr && part == 0) {
-      m[h] = to_f32(Sk[h0 + h]);
-      l[h] = 1.f;
+    for (int c = 0; c < E2; ++c) {
+      qv[h][c] = mul2(sc, tmp[c]);
+      o[h][c] = f2{0};
     }
   }
-
-  if (tid == 0) {
-    for (int st = 0; st < STAGES; ++st) mbar_init(&full[st], 1);
-    fence_barrier_init();
+  // Softmax state of head my_head for this partial.  Lowest finite float, not -inf,
+  // so a fully masked partial stays NaN-free; a sink seeds partial 0.
+  float m = -3.40282347e+38f;
+  float l = 0.f;
+  if (Sk != nullptr && part == 0) {
+    m = to_f32(Sk[h0 + my_head]);
+    l = 1.f;
   }
-  __syncthreads();
 
   auto issue = [&](int blk) {
     const int st = blk % STAGES;
-    const int64_t i0 = static_cast<int64_t>(blk) * PARTIALS;
-    const int64_t rows = (kmax - i0) < PARTIALS ? (kmax - i0) : PARTIALS;
+    const int64_t i0 = static_cast<int64_t>(blk) * KEYS;
+    const int64_t rows = (kmax - i0) < KEYS ? (kmax - i0) : KEYS;
     const uint32_t bytes = static_cast<uint32_t>(rows) * ROW_BYTES;
     mbar_arrive_expect_tx(&full[st], 2 * bytes);
     bulk_load(sK + st * STAGE_ELEMS, Kb + i0 * D, bytes, &full[st]);
     bulk_load(sV + st * STAGE_ELEMS, Vb + i0 * D, bytes, &full[st]);
   };
 
-  int issued = 0;
   if (tid == 0) {
-    for (; issued < STAGES && issued < nblocks; ++issued) issue(issued);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      done_count[st] = 0;
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    int n0 = 0;
+    for (; n0 < STAGES && n0 < nblocks; ++n0) issue(n0);
+    *issued_count = n0;
   }
+  __syncthreads();
 
   bool aborted = false;
   for (int t = 0; t < nblocks; ++t) {
     const int st = t % STAGES;
-    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((t / STAGES) & 1), nullptr);
-    if (!__syncthreads_and(ok)) {
+    bool ok = mbar_wait(&full[st], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (1u << 8) | kErrReasonTimeout);
+      }
       aborted = true;
       break;
     }
-    // Every thread has finished block t-1, so its stage may be refilled.
-    if (tid == 0 && t >= 1 && issued < nblocks) {
-      issue(issued);
-      ++issued;
-    }
-    const int64_t i = static_cast<int64_t>(t) * PARTIALS + part;
-    const bool in_range = i < kmax;
-    float kf[E], vf[E];
-    load_vec<T, E>(sK + st * STAGE_ELEMS + part * D + sub * E, kf);
-    load_vec<T, E>(sV + st * STAGE_ELEMS + part * D + sub * E, vf);
 #pragma unroll
-    for (int h = 0; h < HG; ++h) {
+    for (int r = 0; r < ROWS; ++r) {
+      // key i = t*KEYS + r*PARTIALS + part: partial `part` sees its keys in order
+      const int row = r * PARTIALS + part;
+      const int64_t i = static_cast<int64_t>(t) * KEYS + row;
+      const bool in_range = i < kmax;
+      f2 kf[E2];
+      load_slice<T, E, LP>(sK + st * STAGE_ELEMS + row * D, sub, kf);
+      float dots[HG];
+#pragma unroll
+      for (int h = 0; h < HG; ++h) {
+        // four fp32 chains: pairs c even -> acc[0], c odd -> acc[1]
+        f2 acc[2] = {f2{0}, f2{0}};
+#pragma unroll
+        for (int c = 0; c < E2; ++c) acc[c & 1] = fma2(qv[h][c], kf[c], acc[c & 1]);
+        dots[h] = __fadd_rn(__fadd_rn(lo_of(acc[0]), hi_of(acc[0])),
+                            __fadd_rn(lo_of(acc[1]), hi_of(acc[1])));
+      }
+      const float dot = reduce_heads<LP, HG>(dots, sub);
+
+      // Scalar online-softmax step for head my_head.  ex < 0 marks a skipped key.
       float bias = 0.f;
       bool use = in_range;
       if (p.mask_mode == 2 && in_range) {
-        bias = to_f32(Mk[static_cast<int64_t>(b) * p.ms0 + static_cast<int64_t>(h0 + h) * p.ms1 +
-                         static_cast<int64_t>(s) * p.ms2 + i]);
+        bias = to_f32(mrow[i]);
         use = bias > -3.0e38f;
       }
-      float dot = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) dot = __fmaf_rn(qv[h][e], kf[e], dot);
-#pragma unroll
-      for (int off = LP / 2; off >= 1; off >>= 1) {
-        dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
-      }
+      float ex = -1.f, f = 1.f;
       if (use) {
         const float score = __fadd_rn(dot, bias);
-        if (score > m[h]) {
-          const float f = expf(__fsub_rn(m[h], score));
-          m[h] = score;
-          // e = exp(score - m') = exp(0) = 1
-          l[h] = __fmaf_rn(l[h], f, 1.0f);
-#pragma unroll
-          for (int e = 0; e < E; ++e) o[h][e] = __fmaf_rn(1.0f, vf[e], __fmul_rn(o[h][e], f));
+        if (score > m) {
+          f = expf(__fsub_rn(m, score));
+          m = score;
+          ex = 1.0f;  // exp(score - m') = exp(0)
+          l = __fmaf_rn(l, f, 1.0f);
         } else {
-          const float ex = expf(__fsub_rn(score, m[h]));
-          l[h] = __fadd_rn(l[h], ex);
+          ex = expf(__fsub_rn(score, m));
+          l = __fadd_rn(l, ex);
+        }
+      }
+      const bool any_rescale = __any_sync(0xffffffffu, f != 1.0f);
+
+      f2 vf[E2];
+      load_slice<T, E, LP>(sV + st * STAGE_ELEMS + row * D, sub, vf);
 #pragma unroll
-          for (int e = 0; e < E; ++e) o[h][e] = __fmaf_rn(ex, vf[e], o[h][e]);
+      for (int h = 0; h < HG; ++h) {
+        const int src = part_lane0 + (HG == 1 ? sub : h * (LP / HG));
+        const float eh = HG == 1 ? ex : __shfl_sync(0xffffffffu, ex, src);
+        float fh = 1.f;
+        if (any_rescale) fh = HG == 1 ? f : __shfl_sync(0xffffffffu, f, src);
+        if (!(eh < 0.f)) {
+          if (fh != 1.0f) {
+            const f2 f_2 = pack2(fh, fh);
+#pragma unroll
+            for (int c = 0; c < E2; ++c) o[h][c] = mul2(o[h][c], f_2);
+          }
+          const f2 e_2 = pack2(eh, eh);
+#pragma unroll
+          for (int c = 0; c < E2; ++c) o[h][c] = fma2(e_2, vf[c], o[h][c]);
+        }
+      }
+    }
+    // The last warp to finish with this stage refills it with block t + STAGES; no
+    // warp waits for another.
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&done_count[st], 1) == NW - 1) {
+        __threadfence_block();
+        done_count[st] = 0;
+        if (t + STAGES < nblocks && !*abort_flag) {
+          fence_proxy_async_smem();
+          issue(t + STAGES);
+          atomicMax(issued_count, t + STAGES + 1);
         }
       }
     }
   }
-
-  if (aborted) {
+  if (__syncthreads_or(aborted)) {
     if (tid == 0) {
-      record_error(&g_error_word, (1u << 8) | kErrReasonTimeout);
-      // Drain: wait (bounded) for the copies still in flight before leaving.
-      for (int blk = 0; blk < issued; ++blk) {
+      // Drain: wait (bounded) for the last fill of every stage still in flight.
+      const int issued = *issued_count;
+      for (int blk = issued - STAGES < 0 ? 0 : issued - STAGES; blk < issued; ++blk) {
         mbar_wait(&full[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
       }
     }
     return;
   }
+  __syncthreads();
 
   // ---- combine the 32 partials, one head at a time ----
   T* O = static_cast<T*>(p.out);
@@ -237,10 +415,13 @@ __global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
   for (int h = 0; h < HG; ++h) {
     __syncthreads();  // stage buffers (and the previous head's combine) are free
 #pragma unroll
-    for (int e = 0; e < E; ++e) comb_o[part * D + sub * E + e] = o[h][e];
-    if (sub == 0) {
-      comb_m[part] = m[h];
-      comb_l[part] = l[h];
+    for (int c = 0; c < E2; ++c) {
+      *reinterpret_cast<float2*>(&comb_o[part * D + slice_elem<T, E, LP>(sub, 2 * c)]) =
+          make_float2(lo_of(o[h][c]), hi_of(o[h][c]));
+    }
+    if (sub == h * (LP / HG)) {
+      comb_m[part] = m;
+      comb_l[part] = l;
     }
     __syncthreads();
     for (int j = tid; j < D; j += NT) {
@@ -250,9 +431,9 @@ __global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
       float lsum = 0.f, acc = 0.f;
 #pragma unroll 4
       for (int q = 0; q < PARTIALS; ++q) {
-        const float f = expf(__fsub_rn(comb_m[q], mx));
-        lsum = __fmaf_rn(comb_l[q], f, lsum);
-        acc = __fmaf_rn(comb_o[q * D + j], f, acc);
+        const float fq = expf(__fsub_rn(comb_m[q], mx));
+        lsum = __fmaf_rn(comb_l[q], fq, lsum);
+        acc = __fmaf_rn(comb_o[q * D + j], fq, acc);
       }
       const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
       O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + h) * p.os1 +
@@ -261,30 +442,42 @@ __global__ void __launch_bounds__(PARTIALS * LP) sdpa_kernel(const Params p) {
   }
 }
 
-// Threads per partial: 16-byte vectors per thread where the row allows, a power of
-// two that divides D, at most 32.  A function of (D, dtype) only.
+// Threads per partial: 32 bytes of a key row per thread where the row allows, a power
+// of two that divides D, at most 16 (CTAs of at most 512 threads).  A function of
+// (D, dtype) only.
 template <typename T>
 constexpr int lanes_for(int D) {
-  int lp = (D * static_cast<int>(sizeof(T))) / 16;
-  if (lp > 32) lp = 32;
+  int lp = (D * static_cast<int>(sizeof(T))) / 32;
+  if (lp > 16) lp = 16;
+  if (lp < 1) lp = 1;
   int p2 = 1;
   while (p2 * 2 <= lp) p2 *= 2;
   while (p2 > 1 && D % p2 != 0) p2 /= 2;
   return p2;
 }
 
+// Shared-memory plan per (dtype, D): ROWS key rows per partial per stage and STAGES
+// stages, within ~96 KB of K/V ring (at least 2 stages, at most 4).
+template <typename T, int D>
+constexpr int rows_for() {
+  constexpr int row_pair = 2 * PARTIALS * D * static_cast<int>(sizeof(T));  // K+V, 1 row
+  return (BI_SDPA_ROWS_PER_STAGE * row_pair * 2 <= 128 * 1024) ? BI_SDPA_ROWS_PER_STAGE : 1;
+}
+
 template <typename T, int D>
 constexpr int stages_for() {
-  constexpr int pair = 2 * PARTIALS * D * static_cast<int>(sizeof(T));
+  constexpr int pair = 2 * PARTIALS * rows_for<T, D>() * D * static_cast<int>(sizeof(T));
   constexpr int s = (96 * 1024) / pair;
   return s < 2 ? 2 : (s > 4 ? 4 : s);
 }
 
+// Largest heads-per-CTA the register budget allows: HG * 2E fp32 values of q and o
+// per thread within BI_SDPA_REG_BUDGET.
 template <typename T, int D>
 constexpr int max_heads_per_cta() {
   constexpr int LP = lanes_for<T>(D);
   constexpr int E = D / LP;
-  constexpr int budget = (PARTIALS * LP == 1024) ? 32 : 64;  // registers for q and o
+  constexpr int budget = BI_SDPA_REG_BUDGET;
   return (8 * E <= budget) ? 4 : (4 * E <= budget) ? 2 : 1;
 }
 
@@ -292,22 +485,33 @@ template <typename T, int D, int HG>
 static int launch_hg(const Params& p, int64_t blocks, cudaStream_t stream) {
   constexpr int LP = lanes_for<T>(D);
   constexpr int S = stages_for<T, D>();
+  constexpr int R = rows_for<T, D>();
   constexpr int NT = PARTIALS * LP;
-  constexpr int smem = 2 * S * PARTIALS * D * static_cast<int>(sizeof(T)) + S * 8 +
-                       2 * PARTIALS * 4;
-  static_assert(PARTIALS * D * 4 <= 2 * S * PARTIALS * D * static_cast<int>(sizeof(T)),
+  constexpr int smem = 2 * S * PARTIALS * R * D * static_cast<int>(sizeof(T)) + S * 8 +
+                       4 * (S + 4) + 2 * PARTIALS * 4;
+  static_assert(PARTIALS * D * 4 <= 2 * S * PARTIALS * R * D * static_cast<int>(sizeof(T)),
                 "combine buffer must fit in the stage ring");
-  auto kern = sdpa_kernel<T, D, LP, HG, S>;
+  static_assert(smem <= 227 * 1024, "shared memory above the per-CTA limit");
+  auto kern = sdpa_kernel<T, D, LP, HG, S, R>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa)");
+  // Ask for the largest shared-memory carveout so two CTAs' stage rings fit per SM.
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa carveout)");
   if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "too many attention rows");
   kern<<<static_cast<unsigned>(blocks), NT, smem, stream>>>(p);
   return cuda_status(cudaGetLastError(), "sdpa launch");
 }
 
+#ifndef BI_SDPA_MAX_HG
+#define BI_SDPA_MAX_HG 4
+#endif
+
 template <typename T, int D>
 static int launch_d(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  constexpr int HGMAX = max_heads_per_cta<T, D>();
+  constexpr int HGMAX = max_heads_per_cta<T, D>() < BI_SDPA_MAX_HG ? max_heads_per_cta<T, D>()
+                                                                  : BI_SDPA_MAX_HG;
   const int64_t G = a.H / a.Hkv;
   // Heads per CTA: the largest of {4, 2, 1} within the register budget that divides
   // the GQA factor.  It decides which CTA computes a row, never the row's arithmetic.

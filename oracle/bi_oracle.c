@@ -31,8 +31,10 @@
  * combine with the max over partials, rescale and sum (:125-141); zero output when
  * the denominator is zero (:139).  The reference sums a score with simd_sum over 32
  * lanes in an order Apple does not specify; this restatement splits the head dim
- * over `lanes` threads (sequential fmaf inside a lane, xor-butterfly across lanes)
- * -- the order libbi.so uses -- and states the update formulas as libbi.so does:
+ * over `lanes` threads (each taking interleaved vectors of the row; inside a lane
+ * four fmaf chains summed (c0+c1)+(c2+c3); then an xor-butterfly across lanes) --
+ * the order libbi.so uses --
+ * and states the update formulas as libbi.so does:
  *   m' = max(m, s); f = exp(m - m'); e = exp(s - m'); l = fmaf(l, f, e);
  *   o = fmaf(e, v, o * f); combine: l = sum fmaf(l_p, f_p, .), o = sum fmaf(o_p, f_p, .)
  * exp is the C library's expf, so results match the GPU within a few fp32 ulp, not
@@ -165,7 +167,7 @@ void oracle_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, const v
  * Strides are in elements for (b, h, s) of q/out/mask and (b, h) of k/v; the last
  * dimension of every tensor is contiguous and each (N, D) head block of k and v is
  * row-contiguous.  lanes: threads a key row is split over (a power of two dividing
- * D); D == V.
+ * D, leaving an even count per lane); D == V.
  */
 void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                  const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
@@ -174,6 +176,12 @@ void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t*
                  const int64_t* os, int lanes, int nthreads) {
   const int64_t G = H / Hkv;
   const int64_t E = D / lanes;
+  /* a lane's share of a row: vectors of W bytes (16, 8 or 4, whichever divides its
+     E elements' bytes), the lanes' vectors interleaved: vector c of lane t starts at
+     element (c*lanes + t)*per */
+  const int64_t es = dt == OR_F32 ? 4 : 2;
+  const int64_t vbytes = (E * es) % 16 == 0 ? 16 : ((E * es) % 8 == 0 ? 8 : 4);
+  const int64_t per = vbytes / es;
   const int64_t rows = B * H * qL;
 #ifdef _OPENMP
   if (nthreads > 0) omp_set_num_threads(nthreads);
@@ -226,9 +234,15 @@ void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t*
           vf[j] = load_elem(v, vb + i * D + j, dt);
         }
         for (int t = 0; t < lanes; ++t) {
-          float acc = 0.0f;
-          for (int64_t e = 0; e < E; ++e) acc = fmaf(qv[t * E + e], kf[t * E + e], acc);
-          part[t] = acc;
+          /* four chains -- the lane's e-th element (row element ((e/per)*lanes + t)*per
+             + e%per) goes to chain (e/2 % 2)*2 + e%2 -- summed (c0+c1)+(c2+c3) */
+          float ch[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          for (int64_t e = 0; e < E; ++e) {
+            const int64_t j = ((e / per) * lanes + t) * per + e % per;
+            const int c = (int)(((e / 2) % 2) * 2 + e % 2);
+            ch[c] = fmaf(qv[j], kf[j], ch[c]);
+          }
+          part[t] = (ch[0] + ch[1]) + (ch[2] + ch[3]);
         }
         for (int off = lanes / 2; off >= 1; off /= 2) {
           for (int t = 0; t < lanes; ++t) tmp[t] = part[t] + part[t ^ off];

@@ -87,7 +87,7 @@ def gemm(a, b, bias=None, b_is_nk=False, alpha=1.0, beta=1.0, threads=0):
 def lanes_for(D, dtype):
     """Threads a key row is split over in bi_sdpa (a function of D and dtype only)."""
     es = np.dtype(dtype).itemsize
-    lp = min(32, (D * es) // 16)
+    lp = max(1, min(16, (D * es) // 32))
     p2 = 1
     while p2 * 2 <= lp:
         p2 *= 2

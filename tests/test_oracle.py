@@ -212,12 +212,15 @@ def test_oracle_sdpa_query_length_invariance():
 
 
 def test_lane_split_is_a_function_of_d_and_dtype():
-    assert orc.lanes_for(128, ml_dtypes.bfloat16) == 16
-    assert orc.lanes_for(128, np.float32) == 32
-    assert orc.lanes_for(64, np.float16) == 8
-    assert orc.lanes_for(96, ml_dtypes.bfloat16) == 8
-    assert orc.lanes_for(256, np.float32) == 32
-    assert orc.lanes_for(160, np.float32) == 32
+    assert orc.lanes_for(128, ml_dtypes.bfloat16) == 8
+    assert orc.lanes_for(128, np.float32) == 16
+    assert orc.lanes_for(64, np.float16) == 4
+    assert orc.lanes_for(96, ml_dtypes.bfloat16) == 4
+    assert orc.lanes_for(256, np.float32) == 16
+    assert orc.lanes_for(160, np.float32) == 16
+    for D in range(32, 257, 32):
+        for dt in (np.float32, np.float16):
+            assert (D // orc.lanes_for(D, dt)) % 2 == 0
 
 
 def test_bit_and_ulp_helpers_selftest():
