@@ -2,46 +2,53 @@
 // TMA, for fp16 and bf16 inputs with fp32 accumulation.
 //
 // Invariance argument (the property mlx_batch_invariant/_gemm.py:1-24 states for
-// its Metal kernel): every output element is produced by one CTA that owns the
-// whole K reduction.  The CTA tile (128 x 256), the K block (64) and the UMMA
-// instruction (M=128, N=256, K=16) are compile-time constants, so element (m, n)
-// is always accumulated as the same sequence of K=16 tensor-core steps, k
-// ascending, into an fp32 TMEM accumulator -- for every M, every row position in
-// the tile and every column shard.  There is no split-K, no stream-K and no
-// atomic.  Which CTA takes which tile (the persistent schedule below) changes with
-// M; the arithmetic per element does not.
+// its Metal kernel): every output element is produced by one CTA pair that owns the
+// whole K reduction.  The tile (256 x 256 per pair), the K block (64) and the UMMA
+// instruction (2-SM, M=256, N=256, K=16) are compile-time constants, so element
+// (m, n) is always accumulated as the same sequence of K=16 tensor-core steps, k
+// ascending, into an fp32 TMEM accumulator -- for every M, every row position in the
+// tile and every column shard.  There is no split-K, no stream-K and no atomic.
+// Which pair takes which tile (the persistent schedule below) changes with M; the
+// arithmetic per element does not.
 //
-// Structure: one persistent CTA per SM, 6 warps.
-//   warp 0      TMA producer: A (M x K, K-major) and B tiles into a 4-stage ring.
-//   warp 1      TMEM allocator and UMMA issuer (one thread), two accumulator
-//               buffers of 256 fp32 columns so the epilogue of tile i overlaps the
-//               main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld rows out of TMEM, alpha/bias in fp32, one
-//               rounding to the output type, vector stores.
+// Structure: clusters of two CTAs (a "pair", one per SM) run persistently.  Each CTA
+// loads its own 128 rows of the A tile and its own 128 columns of the B tile with TMA
+// into a 6-stage ring (no multicast); the leader CTA's MMA thread issues 2-SM UMMAs
+// (tcgen05.mma.cta_group::2) that read both CTAs' shared memory and write rows
+// 0-127 of the fp32 accumulator to the leader's TMEM and rows 128-255 to the peer's.
+//   warp 0      TMA producer (both CTAs); the leader's full barrier counts both
+//               CTAs' bytes.
+//   warp 1      TMEM allocator (both CTAs) and, in the leader, the UMMA issuer; two
+//               256-column accumulator buffers so tile i's epilogue overlaps tile
+//               i+1's main loop.  Commits multicast to both CTAs' barriers.
+//   warps 2..5  epilogue (both CTAs): tcgen05.ld of the CTA's 128 rows, alpha/bias in
+//               fp32, one rounding to the output type, vector stores; they release
+//               the accumulator on the leader's barrier.
 // Every mbarrier wait is bounded; a wait that gives up raises the device error word
-// and the CTA drains its own in-flight copies and MMAs, frees TMEM and exits.
-#include <mutex>
-
+// and the CTA drains what it started, frees TMEM and exits.
 #include "common.cuh"
 #include "internal.h"
 
 namespace bi {
 namespace tc {
 
-constexpr int BM = kTcBM;
-constexpr int BN = kTcBN;
-constexpr int BK = kTcBK;  // 64 x 2 bytes = one 128-byte swizzle row
-constexpr int STAGES = 4;
+constexpr int BM = kTcBM;    // rows per CTA (the pair covers 2*BM)
+constexpr int BN = kTcBN;    // columns per pair tile
+constexpr int BN_CTA = BN / 2;  // B columns each CTA loads
+constexpr int BK = kTcBK;    // 64 x 2 bytes = one 128-byte swizzle row
+constexpr int STAGES = 6;
 constexpr int UMMA_K = 16;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
-constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB
+constexpr int B_STAGE_BYTES = BN_CTA * BK * 2;  // 16 KiB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int ACC_BUFS = 2;
 constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512: the whole tensor memory of the SM
 constexpr int NUM_THREADS = 192;
+constexpr int EPI_WARPS = 4;
 constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
 constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES + NUM_BARRIERS * 8 + 16;
-constexpr int GROUP_M = 16;  // tiles of M that consecutive tile indices sweep (L2 reuse)
+constexpr int GROUP_M = 8;  // pair-tiles of M that consecutive tile indices sweep (L2 reuse)
+constexpr uint16_t PAIR_MASK = 0x3;
 
 // Error sites (code = site << 8 | reason).
 enum : unsigned { kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4 };
@@ -69,7 +76,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 }
 
 template <typename T, bool B_NK>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -78,16 +85,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
-  uint64_t* tempty = bars + 2 * STAGES + ACC_BUFS;
+  uint64_t* full = bars;                              // used in the leader
+  uint64_t* empty = bars + STAGES;                    // both CTAs
+  uint64_t* tfull = bars + 2 * STAGES;                // both CTAs
+  uint64_t* tempty = bars + 2 * STAGES + ACC_BUFS;    // used in the leader
   uint64_t* mma_done = bars + 2 * STAGES + 2 * ACC_BUFS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NUM_BARRIERS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -96,7 +107,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < ACC_BUFS; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 2 * EPI_WARPS);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -107,24 +118,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmap_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
   }
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
+      const uint32_t full_leader0 = map_to_cta(smem_u32(&full[0]), 0);
       int stage = 0;
       uint32_t phase = 0;
-      // Parity of the most recent fill of each stage, for the drain on abort.
-      uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      bool issued_any = false;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
         int tm, tn;
         tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -132,21 +144,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(sA + stage * A_STAGE_BYTES, &tmap_a, &full[stage], kb * BK, tm * BM);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          const uint32_t bar = full_leader0 + stage * 8;
+          tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tmap_a, bar, kb * BK,
+                           tm * 2 * BM + static_cast<int>(rank) * BM);
           uint8_t* dstB = sB + stage * B_STAGE_BYTES;
+          const int n0 = tn * BN + static_cast<int>(rank) * BN_CTA;
           if (B_NK) {
-            tma_load_2d(dstB, &tmap_b, &full[stage], kb * BK, tn * BN);
+            tma_load_2d_pair(dstB, &tmap_b, bar, kb * BK, n0);
           } else {
-            // (K, N) row-major B: four 64-column slabs, each 64 k-rows of 128 bytes.
+            // (K, N) row-major B: two 64-column slabs, each 64 k-rows of 128 bytes.
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) {
-              tma_load_2d(dstB + j * (64 * BK * 2), &tmap_b, &full[stage], tn * BN + j * 64,
-                          kb * BK);
+            for (int j = 0; j < BN_CTA / 64; ++j) {
+              tma_load_2d_pair(dstB + j * (64 * BK * 2), &tmap_b, bar, n0 + j * 64, kb * BK);
             }
           }
-          issued_mask |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          issued_any = true;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -156,26 +169,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) {
         *abort_flag = 1;
         record_error(&g_error_word, (kSiteProducer << 8) | kErrReasonTimeout);
-        // Drain: wait (bounded) for every fill this thread started.
-        for (int s = 0; s < STAGES; ++s) {
-          if (issued_mask & (1u << s)) {
-            if (!mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr)) {
-              record_error(&g_error_word, (kSiteDrain << 8) | kErrReasonTimeout);
-            }
-          }
-        }
+        // Drain: the fills complete on the leader's barriers; give them a bounded
+        // moment to land before this CTA's shared memory is released.
+        if (issued_any) sleep_ns(200000);
       }
     }
   } else if (warp == 1) {
-    // ---------------- UMMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- UMMA issuer (leader only) ----------------
+    if (leader && lane == 0) {
       constexpr uint32_t fmt = (dtype_of<T>::value == 2) ? 1u : 0u;
-      constexpr uint32_t idesc = umma_idesc_f16(fmt, B_NK ? 0u : 1u, BM, BN);
+      constexpr uint32_t idesc = umma_idesc_f16(fmt, B_NK ? 0u : 1u, 2 * BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       int it = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs, ++it) {
         const int buf = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
@@ -205,37 +213,38 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               // groups 1024 B apart (SBO); the K=16 step moves 16 rows = 2048 B.
               bdesc = umma_smem_desc(b_base + k * UMMA_K * 128, 64 * BK * 2, 1024, 2);
             }
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+          umma_commit_pair(&empty[stage], PAIR_MASK);  // frees the stage in both CTAs
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[buf]);  // accumulator ready for the epilogue
+        umma_commit_pair(&tfull[buf], PAIR_MASK);  // accumulator ready in both CTAs
       }
       if (!ok) {
         *abort_flag = 1;
         record_error(&g_error_word, (kSiteMma << 8) | kErrReasonTimeout);
       }
       // Whatever happened, wait until every MMA this thread issued has finished
-      // before the CTA releases TMEM and shared memory.
-      umma_commit(mma_done);
+      // before either CTA releases TMEM and shared memory.
+      umma_commit_pair(mma_done, 0x1);
       if (!mbar_wait(mma_done, 0, nullptr)) {
         record_error(&g_error_word, (kSiteDrain << 8) | kErrReasonTimeout);
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter..+31
     const int row_in_tile = quarter * 32 + lane;
     const T* bias = static_cast<const T*>(p.bias);
     T* out = static_cast<T*>(p.out);
     const bool vec_ok = (p.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    const uint32_t tempty_leader0 = map_to_cta(smem_u32(&tempty[0]), 0);
     int it = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+    for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++it) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
       const int buf = it & 1;
@@ -250,7 +259,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tm) * BM + row_in_tile;
+      const int64_t row = static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM +
+                          row_in_tile;
       const bool row_ok = row < p.M;
       T* orow = out + row * p.ldo;
 #pragma unroll 1
@@ -293,16 +303,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // release on the leader
     }
   }
 
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // the leader's MMAs are done and both epilogues have finished
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -315,17 +326,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
+  static EncodeTiledFn fn = [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+      return reinterpret_cast<EncodeTiledFn>(ptr);
     }
-  });
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
   return fn;
 }
 
@@ -359,7 +369,7 @@ static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, BM, g.dtype);
   if (st) return st;
   if (B_NK) {
-    st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, BN, g.dtype);
+    st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, BN_CTA, g.dtype);
   } else {
     st = make_map(&mb, g.b, g.K, g.N, g.ldb, 64, BK, g.dtype);
   }
@@ -381,11 +391,12 @@ static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   p.alpha = g.alpha;
   p.beta = g.beta;
   p.has_bias = g.bias != nullptr;
-  p.tiles_m = static_cast<int>((g.M + BM - 1) / BM);
+  p.tiles_m = static_cast<int>((g.M + 2 * BM - 1) / (2 * BM));
   p.tiles_n = static_cast<int>((g.N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
-  const int grid = p.num_tiles < device_sm_count() ? p.num_tiles : device_sm_count();
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  const int max_pairs = device_sm_count() / 2;
+  const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
+  kern<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
   return cuda_status(cudaGetLastError(), "gemm_tc launch");
 }
 
