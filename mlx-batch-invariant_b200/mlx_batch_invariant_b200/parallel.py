@@ -68,6 +68,18 @@ def gather_columns(y_local, n_total, group=None):
     return out.contiguous()
 
 
+def gather_columns_on(stream, y_local, n_total, group=None, ready=None):
+    """gather_columns issued on `stream` (after `ready`, an event of the stream that
+    produced y_local), so the exchange of one output overlaps the next GEMM on the
+    producing stream.  The result is valid on `stream`; the caller orders its
+    consumers after it (e.g. producer_stream.wait_stream(stream))."""
+    with torch.cuda.stream(stream):
+        if ready is not None:
+            stream.wait_event(ready)
+        y_local.record_stream(stream)
+        return gather_columns(y_local, n_total, group)
+
+
 def column_parallel_linear(x, w_shard, bias_shard, n_total, group=None, local_op=linear):
     """y = x @ w.T + bias over all ranks, w sharded by rows (shard_weight); every rank
     returns the full (..., n_total) output, bitwise equal to a single-GPU linear."""
