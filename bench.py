@@ -7,7 +7,8 @@ A step is one pass of the hot path over config 5 of the build (BASELINE.json
 configs[4]): the invariant GEMM y = bi.linear(x, w) on the four 70B-style (K, N)
 shapes (8192,10240), (8192,8192), (8192,57344), (28672,8192) at M = 4096, bf16,
 x ~ N(0,1), w ~ N(0,0.02) (synthetic, random init), column-parallel over N on N GPUs
-with an NCCL all-gather of the outputs.  `value` is whole-job TFLOP/s (2*M*N*K per
+with the all-gather fused into the GEMM epilogue (parallel.FusedColumnParallel; the
+NCCL all-gather variant is reported beside it as nccl_allgather_tflops).  `value` is whole-job TFLOP/s (2*M*N*K per
 shape, all ranks' columns) over the max-over-ranks device time of exactly K steps.
 The weights (1.7 GB) exceed L2 (126 MB), so no flush is needed between steps.
 
@@ -261,29 +262,39 @@ def run_ours(args):
         w = (torch.randn((e - s, K), generator=gw, device=dev, dtype=torch.float32) * 0.02).to(
             torch.bfloat16)
         ws.append(w)
-    launches_per_step = len(SHAPES)
+    # one GEMM per shape; at N > 1 each fused call also launches its entry barrier
+    launches_per_step = len(SHAPES) * (2 if world > 1 else 1)
 
     comm = torch.cuda.Stream() if world > 1 else None
     main = torch.cuda.current_stream()
+    # At N > 1 the product path is the fused column-parallel GEMM: every rank's
+    # epilogue writes its columns into all ranks' outputs over NVLink.
+    fused = [parallel.FusedColumnParallel(N, M, torch.bfloat16) for _, N in SHAPES] \
+        if world > 1 else None
 
     def step(dom_events=None):
-        # GEMM i runs on the main stream while the all-gather of GEMM i-1's columns
-        # runs on `comm`; the step ends when both streams are done.
         outs = []
         for i, (K, N) in enumerate(SHAPES):
             if dom_events is not None and i == DOMINANT:
                 dom_events[0].record()
-            y = bi.linear(xs[K], ws[i])
+            if world > 1:
+                y = fused[i].linear(xs[K], ws[i])
+            else:
+                y = bi.linear(xs[K], ws[i])
             if dom_events is not None and i == DOMINANT:
                 dom_events[1].record()
-            if world > 1:
-                ready = torch.cuda.Event()
-                ready.record()
-                y = parallel.gather_columns_on(comm, y, N, ready=ready)
             outs.append(y)
-        if world > 1:
-            main.wait_stream(comm)
         return outs
+
+    def nccl_step():
+        # Baseline exchange: GEMM i on the main stream, NCCL all-gather of its columns
+        # on `comm` while GEMM i+1 runs.
+        for i, (K, N) in enumerate(SHAPES):
+            y = bi.linear(xs[K], ws[i])
+            ready = torch.cuda.Event()
+            ready.record()
+            parallel.gather_columns_on(comm, y, N, ready=ready)
+        main.wait_stream(comm)
 
     for _ in range(args.warmup):
         step()
@@ -304,6 +315,20 @@ def run_ours(args):
     ms = e0.elapsed_time(e1)
     ms = _max_over_ranks(ms, world)
     value = FLOPS_PER_STEP * args.steps / (ms / 1e3) / 1e12
+
+    nccl_value = None
+    if world > 1:
+        for _ in range(2):
+            nccl_step()
+        _barrier_sync(world)
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record()
+        for _ in range(args.steps):
+            nccl_step()
+        n1.record()
+        _barrier_sync(world)
+        nccl_ms = _max_over_ranks(n0.elapsed_time(n1), world)
+        nccl_value = FLOPS_PER_STEP * args.steps / (nccl_ms / 1e3) / 1e12
 
     # dominant kernel alone (its own events on its stream), same as in the step
     K, N = SHAPES[DOMINANT]
@@ -348,17 +373,11 @@ def run_ours(args):
     def e2e_step():
         dx = {K: hx[K].to(dev, non_blocking=True) for K in hx}
         for i, (K, N) in enumerate(SHAPES):
-            y = bi.linear(dx[K], ws[i])
             if world > 1:
-                ready = torch.cuda.Event()
-                ready.record()
-                y = parallel.gather_columns_on(comm, y, N, ready=ready)
-                with torch.cuda.stream(comm):
-                    hy[i].copy_(y, non_blocking=True)
+                y = fused[i].linear(dx[K], ws[i])
             else:
-                hy[i].copy_(y, non_blocking=True)
-        if world > 1:
-            main.wait_stream(comm)
+                y = bi.linear(dx[K], ws[i])
+            hy[i].copy_(y, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 10))
     for _ in range(2):
@@ -384,14 +403,17 @@ def run_ours(args):
         "data": "synthetic (random init, seeded)",
         "config": {"workload": "config 5: bi.linear at M=4096 on (K,N) in "
                                "(8192,10240),(8192,8192),(8192,57344),(28672,8192), bf16",
-                   "M": M, "shapes_KN": SHAPES, "parallelism": "column-parallel N over %d GPU%s "
-                   "+ NCCL all-gather" % (world, "s" if world > 1 else ""),
+                   "M": M, "shapes_KN": SHAPES,
+                   "parallelism": ("column-parallel N over %d GPUs, all-gather fused into the "
+                                   "GEMM epilogue (NVLink peer stores)" % world) if world > 1
+                   else "single GPU",
                    "l2": "inputs larger than L2 (1.7 GB of weights), no flush"},
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
         "stock_cublas_tflops": cublas_tflops,
+        "nccl_allgather_tflops": nccl_value,
         "sdpa": sd,
         "clocks": clk,
     }
@@ -400,6 +422,8 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        for f in fused:
+            f.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -119,6 +119,59 @@ int bi_sdpa(const void* q, const int64_t q_strides[3],
             int64_t D, int64_t V, int dtype,
             void* out, const int64_t out_strides[3], void* stream);
 
+/*
+ * ---------------------------------------------------------------------------
+ * Multi-GPU: the column-parallel GEMM with its all-gather fused into the epilogue.
+ *
+ * No reference counterpart (the reference is single-device); this is the exchange
+ * step of the column-parallel plan in which rank r owns columns [col0, col0 + N_local)
+ * of the output.  Instead of a separate all-gather, every CTA stores each finished
+ * output tile into the (M, N_total) output buffer of every rank through NVLink
+ * peer mappings, then ranks exchange epoch flags (bounded waits).  The bits are
+ * those of bi_gemm on the full weight.
+ * ---------------------------------------------------------------------------
+ */
+
+/* Maximum number of ranks bi_gemm_allgather / bi_peer_barrier take. */
+#define BI_MAX_PEERS 8
+
+/* Bytes of the flag block each rank's exchange buffer must end with. */
+#define BI_PEER_FLAG_BYTES 256
+
+/* Allocates `bytes` of device memory that peers may map (zero-filled), and writes
+ * its CUDA IPC handle (64 bytes) to ipc_handle.  Set-up call, not on the hot path. */
+int bi_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+/* Maps a peer's buffer from its IPC handle (another process's bi_peer_alloc). */
+int bi_peer_open(const void* ipc_handle, void** ptr);
+/* Unmaps a buffer mapped with bi_peer_open. */
+int bi_peer_close(void* ptr);
+/* Frees a buffer from bi_peer_alloc (after every peer has unmapped it). */
+int bi_peer_free(void* ptr);
+
+/* Stream-ordered barrier over `world` ranks: rank `rank` posts `epoch` to every
+ * rank's flag block and waits (bounded) until every rank has posted it to its own.
+ * flags[r] is rank r's flag block (BI_PEER_FLAG_BYTES), mapped in this process. */
+int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, void* stream);
+
+/*
+ * Column-parallel y = x . w^T (+ bias) with the all-gather fused into the epilogue.
+ *   a        (M, K) activations, replicated on every rank.
+ *   b        this rank's weight shard: (N_local, K) if b_is_nk, else (K, N_local).
+ *   bias     nullable; this rank's (N_local,) slice.
+ *   outs[r]  rank r's (M, ldo) output buffer mapped here (outs[rank] is local); this
+ *            rank writes columns [col0, col0 + N_local) of every one.
+ *   flags[r] rank r's flag block.  epoch: a value larger than any earlier call's.
+ * On return (stream order) outs[rank] holds all N_total columns.  Calls an entry
+ * barrier first, so no peer still reads the previous contents.  Same arithmetic,
+ * tile and route rules as bi_gemm.
+ */
+int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
+                      const void* bias, void* const* outs, int64_t ldo, int64_t col0,
+                      int64_t M, int64_t N_local, int64_t K, int b_is_nk,
+                      float alpha, float beta, int dtype,
+                      void* const* flags, int rank, int world, uint32_t epoch,
+                      void* stream);
+
 /* Static description of a status code. */
 const char* bi_status_string(int status);
 

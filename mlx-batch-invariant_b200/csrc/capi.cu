@@ -3,6 +3,7 @@
 // gemm_tcgen05.cu, gemm_simt.cu and sdpa.cu.
 #include <stdarg.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <atomic>
 
@@ -205,6 +206,120 @@ int bi_sdpa(const void* q, const int64_t q_strides[3], const void* k, const int6
   a.out = out;
   for (int i = 0; i < 3; ++i) a.os[i] = out_strides[i];
   return launch_sdpa(a, static_cast<cudaStream_t>(stream));
+}
+
+int bi_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+  g_msg[0] = '\0';
+  if (bytes <= 0 || ptr == nullptr || ipc_handle == nullptr) {
+    return set_error(BI_ERR_INVALID, "bi_peer_alloc: bad arguments");
+  }
+  int st = check_device();
+  if (st) return st;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc(peer buffer)");
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(e, "peer buffer set-up");
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return BI_OK;
+}
+
+int bi_peer_open(const void* ipc_handle, void** ptr) {
+  g_msg[0] = '\0';
+  if (ipc_handle == nullptr || ptr == nullptr) return set_error(BI_ERR_INVALID, "bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle");
+}
+
+int bi_peer_close(void* ptr) {
+  g_msg[0] = '\0';
+  return cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+int bi_peer_free(void* ptr) {
+  g_msg[0] = '\0';
+  return cuda_status(cudaFree(ptr), "cudaFree(peer buffer)");
+}
+
+static int gather_args(void* const* outs, void* const* flags, int64_t col0, int rank, int world,
+                       uint32_t epoch, GatherArgs* x) {
+  if (world < 1 || world > BI_MAX_PEERS || rank < 0 || rank >= world || flags == nullptr) {
+    return set_error(BI_ERR_INVALID, "rank %d / world %d outside [0, %d)", rank, world,
+                     BI_MAX_PEERS);
+  }
+  *x = GatherArgs{};
+  for (int r = 0; r < world; ++r) {
+    if (flags[r] == nullptr || (outs != nullptr && outs[r] == nullptr)) {
+      return set_error(BI_ERR_INVALID, "null peer pointer for rank %d", r);
+    }
+    x->flags[r] = static_cast<uint32_t*>(flags[r]);
+    x->outs[r] = outs != nullptr ? outs[r] : nullptr;
+  }
+  x->col0 = col0;
+  x->rank = rank;
+  x->world = world;
+  x->epoch = epoch;
+  return BI_OK;
+}
+
+int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
+  g_msg[0] = '\0';
+  GatherArgs x;
+  int st = gather_args(nullptr, flags, 0, rank, world, epoch, &x);
+  if (st) return st;
+  st = check_device();
+  if (st) return st;
+  return launch_peer_barrier(x, static_cast<cudaStream_t>(stream));
+}
+
+int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
+                      void* const* outs, int64_t ldo, int64_t col0, int64_t M, int64_t N_local,
+                      int64_t K, int b_is_nk, float alpha, float beta, int dtype,
+                      void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather takes fp16 or bf16");
+  }
+  if (M < 0 || N_local < 0 || K < 0 || col0 < 0) return set_error(BI_ERR_INVALID, "negative size");
+  if (outs == nullptr) return set_error(BI_ERR_INVALID, "outs is null");
+  if (col0 % 8 != 0 || ldo % 8 != 0 || col0 + N_local > ldo) {
+    return set_error(BI_ERR_MISALIGNED, "col0 and ldo must be multiples of 8, col0 + N <= ldo");
+  }
+  GatherArgs x;
+  int st = gather_args(outs, flags, col0, rank, world, epoch, &x);
+  if (st) return st;
+  st = check_device();
+  if (st) return st;
+  if (N_local > 0 && M > 0) {
+    if (gemm_route(dtype, K, N_local, b_is_nk) != BI_ROUTE_TCGEN05) {
+      return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather needs the tensor-core route");
+    }
+    if (!aligned16(a) || !aligned16(b) || lda % 8 != 0 || ldb % 8 != 0 || lda < K ||
+        ldb < (b_is_nk ? K : N_local)) {
+      return set_error(BI_ERR_MISALIGNED, "a/b must be 16-byte aligned with 8-element strides");
+    }
+    for (int r = 0; r < world; ++r) {
+      if (!aligned16(outs[r])) return set_error(BI_ERR_MISALIGNED, "output buffers must be aligned");
+    }
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Entry barrier: every rank has finished the work queued before this call (the
+  // readers of the previous contents of its output) before any rank writes into it.
+  st = launch_peer_barrier(x, s);
+  if (st) return st;
+  GemmArgs g{a, lda, b, ldb, bias, outs[rank], ldo, M, N_local, K, b_is_nk ? 1 : 0,
+             alpha, beta, dtype};
+  return launch_gemm_tc_allgather(g, x, s);
 }
 
 const char* bi_status_string(int status) {

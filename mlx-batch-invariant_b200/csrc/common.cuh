@@ -311,6 +311,26 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mas
       : "memory");
 }
 
+// System-scope release store / acquire load of a 32-bit flag (peer memory included).
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Waits (bounded) until the flag at `addr` has reached `epoch` (wrap-safe compare).
+__device__ __forceinline__ bool wait_flag_at_least(const uint32_t* addr, uint32_t epoch) {
+  const long long start = clock64();
+  for (uint32_t it = 0;; ++it) {
+    if (static_cast<int32_t>(ld_acquire_sys(addr) - epoch) >= 0) return true;
+    if ((it & 15u) == 15u && clock64() - start > kWaitBudgetCycles) return false;
+  }
+}
+
 __device__ __forceinline__ void sleep_ns(uint32_t ns) {
   asm volatile("nanosleep.u32 %0;" ::"r"(ns));
 }

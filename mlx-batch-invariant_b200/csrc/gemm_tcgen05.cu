@@ -26,6 +26,13 @@
 //               the accumulator on the leader's barrier.
 // Every mbarrier wait is bounded; a wait that gives up raises the device error word
 // and the CTA drains what it started, frees TMEM and exits.
+//
+// Fused all-gather (GATHER = true, column-parallel over ranks): the epilogue stores
+// each finished 16-byte chunk into every rank's output buffer through NVLink peer
+// mappings (plain stores, no TMA).  Each storing thread fences at system scope; the
+// last CTA of the grid (a counter in the local flag block) then posts the call's epoch
+// to every rank's exit flag with a release store and waits, bounded, until every
+// rank has posted it -- after which this rank's output holds all columns.
 #include "common.cuh"
 #include "internal.h"
 
@@ -46,12 +53,25 @@ constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512: the whole tensor memory of the
 constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARPS = 4;
 constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
-constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES + NUM_BARRIERS * 8 + 16;
+// Epilogue staging: each epilogue warp turns 32 rows x 128 columns of finished outputs
+// around in shared memory so a store instruction writes 256 contiguous bytes of a row.
+constexpr int EPI_COLS = 128;
+constexpr int EPI_STAGE_BYTES = 32 * EPI_COLS * 2;  // per warp, 16-bit outputs
+constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES +
+                           EPI_WARPS * EPI_STAGE_BYTES + NUM_BARRIERS * 8 + 16;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory above the per-CTA limit");
 constexpr int GROUP_M = 8;  // pair-tiles of M that consecutive tile indices sweep (L2 reuse)
 constexpr uint16_t PAIR_MASK = 0x3;
 
 // Error sites (code = site << 8 | reason).
-enum : unsigned { kSiteProducer = 1, kSiteMma = 2, kSiteEpilogue = 3, kSiteDrain = 4 };
+enum : unsigned {
+  kSiteProducer = 1,
+  kSiteMma = 2,
+  kSiteEpilogue = 3,
+  kSiteDrain = 4,
+  kSitePeerExit = 5,
+  kSitePeerEntry = 6
+};
 
 __device__ unsigned g_error_word = 0;
 
@@ -63,6 +83,7 @@ struct Params {
   float alpha, beta;
   int has_bias;
   int tiles_m, tiles_n, num_tiles;
+  GatherArgs gx;  // used when GATHER
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -75,7 +96,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   tn = in_group / rows;
 }
 
-template <typename T, bool B_NK>
+template <typename T, bool B_NK, bool GATHER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const Params p) {
@@ -84,7 +105,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi_stage = smem + STAGES * STAGE_BYTES;  // EPI_WARPS x EPI_STAGE_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + EPI_WARPS * EPI_STAGE_BYTES);
   uint64_t* full = bars;                              // used in the leader
   uint64_t* empty = bars + STAGES;                    // both CTAs
   uint64_t* tfull = bars + 2 * STAGES;                // both CTAs
@@ -259,52 +281,131 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM +
-                          row_in_tile;
+      const int64_t row_base =
+          static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + quarter * 32;
+      const int64_t row = row_base + lane;
       const bool row_ok = row < p.M;
       T* orow = out + row * p.ldo;
+      uint8_t* stg = epi_stage + (warp - 2) * EPI_STAGE_BYTES;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-        tmem_ld_32x32b_x32(tmem_base + buf * BN + c + (static_cast<uint32_t>(quarter * 32) << 16),
-                           r);
-        tmem_ld_wait();
-        const int col0 = tn * BN + c;
-        if (!row_ok || col0 >= p.N) continue;
-        if (vec_ok && col0 + 32 <= p.N) {
-          uint32_t packed[16];
+      for (int h = 0; h < BN; h += EPI_COLS) {
+        const int hcol = tn * BN + h;  // first (local) column of this half tile
+        // Full 128-column halves go through the staging buffer; ragged edges and
+        // unaligned outputs take the per-thread path.
+        const bool staged = vec_ok && hcol + EPI_COLS <= p.N;
+#pragma unroll 1
+        for (int c = 0; c < EPI_COLS; c += 32) {
+          uint32_t r[32];
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+          tmem_ld_32x32b_x32(
+              tmem_base + buf * BN + h + c + (static_cast<uint32_t>(quarter * 32) << 16), r);
+          tmem_ld_wait();
+          const int col0 = hcol + c;
+          if (staged) {
+            uint32_t packed[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const float b0 = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
-            const float b1 = p.has_bias ? to_f32(bias[col0 + j + 1]) : 0.f;
-            const T lo = gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, b0);
-            const T hi =
-                gemm_epilogue<T>(__uint_as_float(r[j + 1]), p.has_bias, p.alpha, p.beta, b1);
-            packed[j / 2] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
-                            (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            for (int j = 0; j < 32; j += 2) {
+              const float b0 = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
+              const float b1 = p.has_bias ? to_f32(bias[col0 + j + 1]) : 0.f;
+              const T lo = gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, b0);
+              const T hi =
+                  gemm_epilogue<T>(__uint_as_float(r[j + 1]), p.has_bias, p.alpha, p.beta, b1);
+              packed[j / 2] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                              (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            }
+            // Row `lane` of the stage, 16-byte chunk u stored at u ^ (lane & 15).
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int u = (c >> 3) + q;
+              *reinterpret_cast<uint4*>(stg + lane * (EPI_COLS * 2) + ((u ^ (lane & 15)) << 4)) =
+                  make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                             packed[4 * q + 3]);
+            }
+            continue;
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+          if (!row_ok || col0 >= p.N) continue;
+          if (vec_ok && col0 + 32 <= p.N) {
+            uint32_t packed[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
-                                packed[4 * q + 3]);
-          }
-        } else {
+            for (int j = 0; j < 32; j += 2) {
+              const float b0 = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
+              const float b1 = p.has_bias ? to_f32(bias[col0 + j + 1]) : 0.f;
+              const T lo = gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, b0);
+              const T hi =
+                  gemm_epilogue<T>(__uint_as_float(r[j + 1]), p.has_bias, p.alpha, p.beta, b1);
+              packed[j / 2] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                              (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+            }
+            if constexpr (GATHER) {
+              const int64_t off = row * p.ldo + p.gx.col0 + col0;
+              for (int j = 0; j < p.gx.world; ++j) {
+                int rr = p.gx.rank + j;
+                if (rr >= p.gx.world) rr -= p.gx.world;
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.gx.outs[rr]) + off);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) {
-              const float bj = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
-              orow[col0 + j] =
-                  gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, bj);
+                for (int q = 0; q < 4; ++q) {
+                  dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                                      packed[4 * q + 3]);
+                }
+              }
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
+                                    packed[4 * q + 3]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < p.N) {
+                const float bj = p.has_bias ? to_f32(bias[col0 + j]) : 0.f;
+                const T v =
+                    gemm_epilogue<T>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, bj);
+                if constexpr (GATHER) {
+                  const int64_t off = row * p.ldo + p.gx.col0 + col0 + j;
+                  for (int q = 0; q < p.gx.world; ++q) static_cast<T*>(p.gx.outs[q])[off] = v;
+                } else {
+                  orow[col0 + j] = v;
+                }
+              }
             }
           }
+        }
+        if (staged) {
+          // Write the staged 32 x 128 block: two rows per instruction, 16 threads x 16 B
+          // = 256 contiguous bytes per row (into every rank's output when gathering).
+          __syncwarp();
+          const int half_row = lane >> 4;
+          const int u = lane & 15;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; rr += 2) {
+            const int lr = rr + half_row;
+            const int64_t grow = row_base + lr;
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(stg + lr * (EPI_COLS * 2) + ((u ^ (lr & 15)) << 4));
+            if (grow < p.M) {
+              if constexpr (GATHER) {
+                const int64_t off = grow * p.ldo + p.gx.col0 + hcol + u * 8;
+                for (int j = 0; j < p.gx.world; ++j) {
+                  int dr = p.gx.rank + j;
+                  if (dr >= p.gx.world) dr -= p.gx.world;
+                  *reinterpret_cast<uint4*>(static_cast<T*>(p.gx.outs[dr]) + off) = v;
+                }
+              } else {
+                *reinterpret_cast<uint4*>(out + grow * p.ldo + hcol + u * 8) = v;
+              }
+            }
+          }
+          __syncwarp();  // the stage is rewritten by the next half
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // release on the leader
     }
+    if constexpr (GATHER) __threadfence_system();  // this thread's peer stores, before the flag
   }
 
   __syncwarp();
@@ -314,6 +415,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  if constexpr (GATHER) {
+    if (threadIdx.x == 0) {
+      // Every CTA's stores are fenced; the last CTA to count itself in publishes the
+      // epoch to every rank and waits for every rank's.
+      uint32_t* counter = p.gx.flags[p.gx.rank] + kFlagCounter;
+      __threadfence_system();
+      if (atomicAdd(counter, 1u) == gridDim.x - 1) {
+        *counter = 0;  // the next call's CTAs start from zero (stream order)
+        __threadfence_system();
+        for (int r = 0; r < p.gx.world; ++r) {
+          st_release_sys(p.gx.flags[r] + kFlagExit + p.gx.rank, p.gx.epoch);
+        }
+        for (int r = 0; r < p.gx.world; ++r) {
+          if (!wait_flag_at_least(p.gx.flags[p.gx.rank] + kFlagExit + r, p.gx.epoch)) {
+            record_error(&g_error_word, (kSitePeerExit << 8) | kErrReasonTimeout);
+            break;
+          }
+        }
+      }
+    }
+  }
+}
+
+// Stream-ordered barrier over the ranks of a GatherArgs (one warp): post the epoch to
+// every rank's flag `slot` (entry or exit), then wait (bounded) for every rank's.
+__global__ void peer_barrier_kernel(const GatherArgs x, int slot) {
+  const int t = threadIdx.x;
+  __threadfence_system();
+  if (t < x.world) st_release_sys(x.flags[t] + slot + x.rank, x.epoch);
+  __syncwarp();
+  bool ok = true;
+  if (t < x.world) ok = wait_flag_at_least(x.flags[x.rank] + slot + t, x.epoch);
+  if (!ok) {
+    record_error(&g_error_word,
+                 ((slot == kFlagEntry ? kSitePeerEntry : kSitePeerExit) << 8) | kErrReasonTimeout);
   }
 }
 
@@ -363,8 +500,8 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
   return BI_OK;
 }
 
-template <typename T, bool B_NK>
-static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
+template <typename T, bool B_NK, bool GATHER>
+static int launch_typed(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
   CUtensorMap ma, mb;
   int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, BM, g.dtype);
   if (st) return st;
@@ -375,7 +512,7 @@ static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   }
   if (st) return st;
 
-  auto kern = gemm_tc_kernel<T, B_NK>;
+  auto kern = gemm_tc_kernel<T, B_NK, GATHER>;
   // The attribute is per device; setting it again is cheap and capture-safe.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES);
@@ -394,10 +531,28 @@ static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   p.tiles_m = static_cast<int>((g.M + 2 * BM - 1) / (2 * BM));
   p.tiles_n = static_cast<int>((g.N + BN - 1) / BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
+  if (gx != nullptr) {
+    p.gx = *gx;
+  } else {
+    p.gx = GatherArgs{};
+  }
   const int max_pairs = device_sm_count() / 2;
   const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
   kern<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
   return cuda_status(cudaGetLastError(), "gemm_tc launch");
+}
+
+template <bool GATHER>
+static int dispatch(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
+  if (g.dtype == BI_BF16) {
+    return g.b_is_nk ? launch_typed<__nv_bfloat16, true, GATHER>(g, gx, stream)
+                     : launch_typed<__nv_bfloat16, false, GATHER>(g, gx, stream);
+  }
+  if (g.dtype == BI_F16) {
+    return g.b_is_nk ? launch_typed<__half, true, GATHER>(g, gx, stream)
+                     : launch_typed<__half, false, GATHER>(g, gx, stream);
+  }
+  return set_error(BI_ERR_UNSUPPORTED, "tensor-core route takes fp16 or bf16");
 }
 
 }  // namespace tc
@@ -406,15 +561,25 @@ int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) {
   if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) {
     return set_error(BI_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
   }
-  if (g.dtype == BI_BF16) {
-    return g.b_is_nk ? tc::launch_typed<__nv_bfloat16, true>(g, stream)
-                     : tc::launch_typed<__nv_bfloat16, false>(g, stream);
+  return tc::dispatch<false>(g, nullptr, stream);
+}
+
+int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, cudaStream_t stream) {
+  if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) {
+    return set_error(BI_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
   }
-  if (g.dtype == BI_F16) {
-    return g.b_is_nk ? tc::launch_typed<__half, true>(g, stream)
-                     : tc::launch_typed<__half, false>(g, stream);
+  if (g.M == 0 || g.N == 0) {
+    // An empty shard computes nothing but still posts and awaits the exit epoch the
+    // peers' GEMMs wait for.
+    tc::peer_barrier_kernel<<<1, 32, 0, stream>>>(x, kFlagExit);
+    return cuda_status(cudaGetLastError(), "peer exit launch");
   }
-  return set_error(BI_ERR_UNSUPPORTED, "tensor-core route takes fp16 or bf16");
+  return tc::dispatch<true>(g, &x, stream);
+}
+
+int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream) {
+  tc::peer_barrier_kernel<<<1, 32, 0, stream>>>(x, kFlagEntry);
+  return cuda_status(cudaGetLastError(), "peer barrier launch");
 }
 
 unsigned read_error_gemm_tc(bool clear) {

@@ -22,6 +22,21 @@ struct GemmArgs {
   int dtype;
 };
 
+// Column-parallel GEMM with the all-gather fused into the epilogue.
+struct GatherArgs {
+  void* outs[BI_MAX_PEERS];       // every rank's (M, ldo) output, mapped here
+  uint32_t* flags[BI_MAX_PEERS];  // every rank's flag block, mapped here
+  int64_t col0;                   // first global column of this rank's shard
+  int rank, world;
+  uint32_t epoch;
+};
+
+// Flag block layout (32-bit words): [0, 8) exit flags posted by rank r, [8, 16) entry
+// flags posted by rank r, [16] CTA-completion counter of the local GEMM.
+constexpr int kFlagExit = 0;
+constexpr int kFlagEntry = BI_MAX_PEERS;
+constexpr int kFlagCounter = 2 * BI_MAX_PEERS;
+
 struct SdpaArgs {
   const void* q;
   int64_t qs[3];
@@ -51,6 +66,8 @@ constexpr int kSimtBN = 128;
 constexpr int kSimtBK = 8;
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
+int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, cudaStream_t stream);
+int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
 int launch_sdpa(const SdpaArgs& s, cudaStream_t stream);
 

@@ -84,6 +84,20 @@ def _distributed_checks(dtypes, gen_seed, dev):
             if rank == 0:
                 print("  %-9s linear   K=%-6d N=%-6d g=%d %s"
                       % (name, K, N, world, "ok" if ok else "VARIANT across GPU count"))
+            if dtype != torch.float32:
+                fused = parallel.FusedColumnParallel(N, 64, dtype)
+                try:
+                    ok = True
+                    for rows in (33, 1, 64):  # several calls reuse the exchange buffer
+                        xr = x[:rows] if rows <= 33 else torch.cat([x, x[:31]])
+                        y = fused.linear(xr, ws, bs)
+                        ok = ok and torch.equal(_bits(y), _bits(linear(xr, w, b)))
+                finally:
+                    fused.close()
+                fails += not ok
+                if rank == 0:
+                    print("  %-9s linear   K=%-6d N=%-6d g=%d fused all-gather %s"
+                          % (name, K, N, world, "ok" if ok else "VARIANT across GPU count"))
         H, Hkv = 32, 8
         if Hkv % world == 0:
             q = _randn((2, H, 3, 128), dtype, gen, dev)

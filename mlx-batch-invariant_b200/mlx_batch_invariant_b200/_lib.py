@@ -16,6 +16,8 @@ BI_F32, BI_F16, BI_BF16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: BI_F32, torch.float16: BI_F16, torch.bfloat16: BI_BF16}
 
 ROUTE_TCGEN05, ROUTE_SIMT = 0, 1
+MAX_PEERS = 8          # BI_MAX_PEERS
+PEER_FLAG_BYTES = 256  # BI_PEER_FLAG_BYTES
 
 _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
@@ -56,6 +58,22 @@ def _bind(lib):
     lib.bi_device_error.argtypes = [ctypes.c_int]
     lib.bi_version.restype = ctypes.c_int
     lib.bi_version.argtypes = []
+    lib.bi_peer_alloc.restype = ctypes.c_int
+    lib.bi_peer_alloc.argtypes = [_i64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
+    lib.bi_peer_open.restype = ctypes.c_int
+    lib.bi_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.bi_peer_close.restype = ctypes.c_int
+    lib.bi_peer_close.argtypes = [_vp]
+    lib.bi_peer_free.restype = ctypes.c_int
+    lib.bi_peer_free.argtypes = [_vp]
+    lib.bi_peer_barrier.restype = ctypes.c_int
+    lib.bi_peer_barrier.argtypes = [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_uint32, _vp]
+    lib.bi_gemm_allgather.restype = ctypes.c_int
+    lib.bi_gemm_allgather.argtypes = [_vp, _i64, _vp, _i64, _vp, ctypes.POINTER(_vp), _i64, _i64,
+                                      _i64, _i64, _i64, ctypes.c_int, ctypes.c_float,
+                                      ctypes.c_float, ctypes.c_int, ctypes.POINTER(_vp),
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _vp]
 
 
 def lib():
