@@ -172,6 +172,40 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
                       void* const* flags, int rank, int world, uint32_t epoch,
                       void* stream);
 
+/*
+ * bi_gemm_allgather for callers that may not allocate device memory.  No counterpart
+ * in the reference (which is single-device).
+ *
+ * bi_gemm_allgather needs a flag block per rank from bi_peer_alloc, which calls
+ * cudaMalloc.  Some callers cannot do that: a serving process whose device memory is
+ * all handed out up front by its own allocator (weights, KV cache, activation arena)
+ * and which must not have a library take memory behind that allocator's back, or a
+ * host program that only ever passes buffers it owns.  This entry point takes no
+ * flag blocks: each rank's block is its device's copy of a 256-byte file-scope
+ * device array inside libbi.so (BI_PEER_FLAG_BYTES per device, held by every GPU that
+ * loads the library until the process exits).  Everything else is as in
+ * bi_gemm_allgather, and it calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ *   devices[r]  the CUDA device ordinal rank r runs on, all in THIS process (one
+ *               process drives every rank, with peer access enabled between them);
+ *               outs[r] must be addressable from each of these devices.
+ *   world       at most BI_MAX_PEERS; larger values are rejected (BI_ERR_INVALID)
+ *               because the static block holds flags for BI_MAX_PEERS ranks.
+ *
+ * The first call that names a device looks up its copy of the array with that
+ * device current (cudaGetSymbolAddress) and caches the address; make that first call
+ * before any stream capture.  All calls on a device share its block, which keeps the
+ * last call's contents: each call clears the block's CTA counter on `stream` before
+ * use, and `epoch` must exceed the epoch of every earlier call on the same devices.
+ * Calls whose work overlaps on the GPU (different streams, or different rank groups
+ * sharing a device) race on the block.
+ */
+int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,
+                             const void* bias, void* const* outs, int64_t ldo, int64_t col0,
+                             int64_t M, int64_t N_local, int64_t K, int b_is_nk,
+                             float alpha, float beta, int dtype, const int* devices,
+                             int rank, int world, uint32_t epoch, void* stream);
+
 /* Static description of a status code. */
 const char* bi_status_string(int status);
 

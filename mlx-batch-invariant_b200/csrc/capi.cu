@@ -322,6 +322,35 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, co
   return launch_gemm_tc_allgather(g, x, s);
 }
 
+int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,
+                             const void* bias, void* const* outs, int64_t ldo, int64_t col0,
+                             int64_t M, int64_t N_local, int64_t K, int b_is_nk, float alpha,
+                             float beta, int dtype, const int* devices, int rank, int world,
+                             uint32_t epoch, void* stream) {
+  g_msg[0] = '\0';
+  if (world < 1 || world > BI_MAX_PEERS) {
+    return set_error(BI_ERR_INVALID,
+                     "bi_gemm_allgather_static: world %d outside [1, %d] -- the static flag "
+                     "block holds flags for at most %d ranks",
+                     world, BI_MAX_PEERS, BI_MAX_PEERS);
+  }
+  if (devices == nullptr) return set_error(BI_ERR_INVALID, "devices is null");
+  // Each rank's flag block is its device's copy of the library's static array.
+  void* flags[BI_MAX_PEERS] = {};
+  for (int r = 0; r < world; ++r) {
+    const int st = static_flag_block(devices[r], &flags[r]);
+    if (st) return st;
+  }
+  if (rank < 0 || rank >= world) return set_error(BI_ERR_INVALID, "rank outside [0, world)");
+  // The block keeps the previous call's contents; the CTA counter must start at zero.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(static_cast<uint32_t*>(flags[rank]) + kFlagCounter, 0,
+                                  sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_status(e, "clearing the static CTA counter");
+  return bi_gemm_allgather(a, lda, b, ldb, bias, outs, ldo, col0, M, N_local, K, b_is_nk, alpha,
+                           beta, dtype, flags, rank, world, epoch, stream);
+}
+
 const char* bi_status_string(int status) {
   switch (status) {
     case BI_OK: return "ok";

@@ -33,10 +33,19 @@
 // last CTA of the grid (a counter in the local flag block) then posts the call's epoch
 // to every rank's exit flag with a release store and waits, bounded, until every
 // rank has posted it -- after which this rank's output holds all columns.
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace bi {
+
+// Scratch of bi_gemm_allgather_static: the epoch-flag block (exit and entry flags and
+// the CTA counter) kept in a file-scope device array instead of caller-allocated
+// memory.  Every device that loads this library holds its own 256-byte copy until the
+// process exits; all calls on a device share it.
+static __device__ __align__(256) uint32_t g_static_flag_block[BI_PEER_FLAG_BYTES / 4];
+
 namespace tc {
 
 constexpr int BM = kTcBM;    // rows per CTA (the pair covers 2*BM)
@@ -580,6 +589,33 @@ int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, cudaStream_
 int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream) {
   tc::peer_barrier_kernel<<<1, 32, 0, stream>>>(x, kFlagEntry);
   return cuda_status(cudaGetLastError(), "peer barrier launch");
+}
+
+// Device address of `device`'s copy of g_static_flag_block.  Looked up once per device,
+// with that device current (the host-side name of a __device__ array is only a
+// stand-in for it), then cached.
+int static_flag_block(int device, void** out) {
+  static std::mutex mu;
+  static void* cache[64] = {};
+  if (device < 0 || device >= 64) return set_error(BI_ERR_INVALID, "device %d out of range", device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == nullptr) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    if (cur != device) {
+      e = cudaSetDevice(device);
+      if (e != cudaSuccess) return cuda_status(e, "cudaSetDevice(static flag block)");
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_flag_block);
+    const cudaError_t back = cur != device ? cudaSetDevice(cur) : cudaSuccess;
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(static flag block)");
+    if (back != cudaSuccess) return cuda_status(back, "cudaSetDevice(restore)");
+    cache[device] = p;
+  }
+  *out = cache[device];
+  return BI_OK;
 }
 
 unsigned read_error_gemm_tc(bool clear) {

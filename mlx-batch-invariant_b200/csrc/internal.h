@@ -68,6 +68,7 @@ constexpr int kSimtBK = 8;
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
 int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, cudaStream_t stream);
 int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream);
+int static_flag_block(int device, void** out);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
 int launch_sdpa(const SdpaArgs& s, cudaStream_t stream);
 
