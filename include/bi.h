@@ -124,11 +124,12 @@ int bi_sdpa(const void* q, const int64_t q_strides[3],
  * Multi-GPU: the column-parallel GEMM with its all-gather fused into the epilogue.
  *
  * No reference counterpart (the reference is single-device); this is the exchange
- * step of the column-parallel plan in which rank r owns columns [col0, col0 + N_local)
- * of the output.  Instead of a separate all-gather, every CTA stores each finished
- * output tile into the (M, N_total) output buffer of every rank through NVLink
- * peer mappings, then ranks exchange epoch flags (bounded waits).  The bits are
- * those of bi_gemm on the full weight.
+ * step of the column-parallel plan in which rank s owns output columns
+ * [cols[s], cols[s+1]).  Instead of a separate all-gather, every CTA stores each
+ * finished output tile into this rank's output and, through NVLink peer mappings,
+ * into every other rank's staging area as part of one dense (M, N_local) block; ranks
+ * then exchange epoch flags (bounded waits) and each copies the blocks it received
+ * into its output.  The bits are those of bi_gemm on the full weight.
  * ---------------------------------------------------------------------------
  */
 
@@ -155,19 +156,25 @@ int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, voi
 
 /*
  * Column-parallel y = x . w^T (+ bias) with the all-gather fused into the epilogue.
- *   a        (M, K) activations, replicated on every rank.
- *   b        this rank's weight shard: (N_local, K) if b_is_nk, else (K, N_local).
- *   bias     nullable; this rank's (N_local,) slice.
- *   outs[r]  rank r's (M, ldo) output buffer mapped here (outs[rank] is local); this
- *            rank writes columns [col0, col0 + N_local) of every one.
- *   flags[r] rank r's flag block.  epoch: a value larger than any earlier call's.
- * On return (stream order) outs[rank] holds all N_total columns.  Calls an entry
- * barrier first, so no peer still reads the previous contents.  Same arithmetic,
+ *   a          (M, K) activations, replicated on every rank.
+ *   b          this rank's weight shard: (N_local, K) if b_is_nk, else (K, N_local),
+ *              N_local = cols[rank+1] - cols[rank].
+ *   bias       nullable; this rank's (N_local,) slice.
+ *   out        this rank's (M, ldo) output, any device memory of this rank (it is only
+ *              written locally); ldo >= cols[world], a multiple of 8.
+ *   stages[r]  rank r's staging area mapped here (stages[rank] is local): at least
+ *              M * cols[world] elements; rank s writes its block (M, N_s) row-major at
+ *              element offset M * cols[s] of every other rank's area.
+ *   cols       world + 1 column bounds: cols[0] = 0, nondecreasing, multiples of 8.
+ *   flags[r]   rank r's flag block.  epoch: a value larger than any earlier call's.
+ * On return (stream order) `out` holds all cols[world] columns.  Calls an entry barrier
+ * first, so no peer writes a staging area its owner may still read.  Same arithmetic,
  * tile and route rules as bi_gemm.
  */
 int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
-                      const void* bias, void* const* outs, int64_t ldo, int64_t col0,
-                      int64_t M, int64_t N_local, int64_t K, int b_is_nk,
+                      const void* bias, void* out, int64_t ldo,
+                      void* const* stages, const int64_t* cols,
+                      int64_t M, int64_t K, int b_is_nk,
                       float alpha, float beta, int dtype,
                       void* const* flags, int rank, int world, uint32_t epoch,
                       void* stream);
@@ -188,7 +195,7 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
  *
  *   devices[r]  the CUDA device ordinal rank r runs on, all in THIS process (one
  *               process drives every rank, with peer access enabled between them);
- *               outs[r] must be addressable from each of these devices.
+ *               stages[r] must be addressable from each of these devices.
  *   world       at most BI_MAX_PEERS; larger values are rejected (BI_ERR_INVALID)
  *               because the static block holds flags for BI_MAX_PEERS ranks.
  *
@@ -201,8 +208,9 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
  * sharing a device) race on the block.
  */
 int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,
-                             const void* bias, void* const* outs, int64_t ldo, int64_t col0,
-                             int64_t M, int64_t N_local, int64_t K, int b_is_nk,
+                             const void* bias, void* out, int64_t ldo,
+                             void* const* stages, const int64_t* cols,
+                             int64_t M, int64_t K, int b_is_nk,
                              float alpha, float beta, int dtype, const int* devices,
                              int rank, int world, uint32_t epoch, void* stream);
 

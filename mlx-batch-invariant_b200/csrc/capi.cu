@@ -251,21 +251,33 @@ int bi_peer_free(void* ptr) {
   return cuda_status(cudaFree(ptr), "cudaFree(peer buffer)");
 }
 
-static int gather_args(void* const* outs, void* const* flags, int64_t col0, int rank, int world,
-                       uint32_t epoch, GatherArgs* x) {
+// Validates the rank set and (when given) the staging areas and the column partition.
+static int gather_args(void* const* stages, void* const* flags, const int64_t* cols, int rank,
+                       int world, uint32_t epoch, GatherArgs* x) {
   if (world < 1 || world > BI_MAX_PEERS || rank < 0 || rank >= world || flags == nullptr) {
     return set_error(BI_ERR_INVALID, "rank %d / world %d outside [0, %d)", rank, world,
                      BI_MAX_PEERS);
   }
   *x = GatherArgs{};
   for (int r = 0; r < world; ++r) {
-    if (flags[r] == nullptr || (outs != nullptr && outs[r] == nullptr)) {
+    if (flags[r] == nullptr || (stages != nullptr && stages[r] == nullptr)) {
       return set_error(BI_ERR_INVALID, "null peer pointer for rank %d", r);
     }
     x->flags[r] = static_cast<uint32_t*>(flags[r]);
-    x->outs[r] = outs != nullptr ? outs[r] : nullptr;
+    x->stages[r] = stages != nullptr ? stages[r] : nullptr;
   }
-  x->col0 = col0;
+  if (cols != nullptr) {
+    if (cols[0] != 0) return set_error(BI_ERR_INVALID, "cols[0] must be 0");
+    for (int r = 0; r <= world; ++r) {
+      if (r > 0 && cols[r] < cols[r - 1]) {
+        return set_error(BI_ERR_INVALID, "cols must be nondecreasing");
+      }
+      if (cols[r] % 8 != 0) {
+        return set_error(BI_ERR_MISALIGNED, "column bounds must be multiples of 8");
+      }
+      x->cols[r] = cols[r];
+    }
+  }
   x->rank = rank;
   x->world = world;
   x->epoch = epoch;
@@ -275,7 +287,7 @@ static int gather_args(void* const* outs, void* const* flags, int64_t col0, int 
 int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
   g_msg[0] = '\0';
   GatherArgs x;
-  int st = gather_args(nullptr, flags, 0, rank, world, epoch, &x);
+  int st = gather_args(nullptr, flags, nullptr, rank, world, epoch, &x);
   if (st) return st;
   st = check_device();
   if (st) return st;
@@ -283,48 +295,57 @@ int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, voi
 }
 
 int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
-                      void* const* outs, int64_t ldo, int64_t col0, int64_t M, int64_t N_local,
-                      int64_t K, int b_is_nk, float alpha, float beta, int dtype,
+                      void* out, int64_t ldo, void* const* stages, const int64_t* cols,
+                      int64_t M, int64_t K, int b_is_nk, float alpha, float beta, int dtype,
                       void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
   g_msg[0] = '\0';
   if (dtype != BI_F16 && dtype != BI_BF16) {
     return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather takes fp16 or bf16");
   }
-  if (M < 0 || N_local < 0 || K < 0 || col0 < 0) return set_error(BI_ERR_INVALID, "negative size");
-  if (outs == nullptr) return set_error(BI_ERR_INVALID, "outs is null");
-  if (col0 % 8 != 0 || ldo % 8 != 0 || col0 + N_local > ldo) {
-    return set_error(BI_ERR_MISALIGNED, "col0 and ldo must be multiples of 8, col0 + N <= ldo");
+  if (M < 0 || K < 0) return set_error(BI_ERR_INVALID, "negative size");
+  if (stages == nullptr || cols == nullptr) {
+    return set_error(BI_ERR_INVALID, "stages and cols must not be null");
   }
   GatherArgs x;
-  int st = gather_args(outs, flags, col0, rank, world, epoch, &x);
+  int st = gather_args(stages, flags, cols, rank, world, epoch, &x);
   if (st) return st;
+  const int64_t n_total = x.cols[world];
+  const int64_t n_local = x.cols[rank + 1] - x.cols[rank];
+  if (ldo % 8 != 0 || ldo < n_total) {
+    return set_error(BI_ERR_MISALIGNED, "ldo must be a multiple of 8 and at least cols[world]");
+  }
   st = check_device();
   if (st) return st;
-  if (N_local > 0 && M > 0) {
-    if (gemm_route(dtype, K, N_local, b_is_nk) != BI_ROUTE_TCGEN05) {
+  if (M > 0 && n_total > 0) {
+    if (!aligned16(out)) return set_error(BI_ERR_MISALIGNED, "out must be 16-byte aligned");
+    for (int r = 0; r < world; ++r) {
+      if (!aligned16(stages[r])) return set_error(BI_ERR_MISALIGNED, "staging areas must be aligned");
+    }
+  }
+  if (n_local > 0 && M > 0) {
+    if (gemm_route(dtype, K, n_local, b_is_nk) != BI_ROUTE_TCGEN05) {
       return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather needs the tensor-core route");
     }
     if (!aligned16(a) || !aligned16(b) || lda % 8 != 0 || ldb % 8 != 0 || lda < K ||
-        ldb < (b_is_nk ? K : N_local)) {
+        ldb < (b_is_nk ? K : n_local)) {
       return set_error(BI_ERR_MISALIGNED, "a/b must be 16-byte aligned with 8-element strides");
-    }
-    for (int r = 0; r < world; ++r) {
-      if (!aligned16(outs[r])) return set_error(BI_ERR_MISALIGNED, "output buffers must be aligned");
     }
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Entry barrier: every rank has finished the work queued before this call (the
-  // readers of the previous contents of its output) before any rank writes into it.
+  // unpack that read the previous contents of its staging area) before any rank
+  // writes into it.
   st = launch_peer_barrier(x, s);
   if (st) return st;
-  GemmArgs g{a, lda, b, ldb, bias, outs[rank], ldo, M, N_local, K, b_is_nk ? 1 : 0,
+  void* out_shard = out != nullptr ? static_cast<uint16_t*>(out) + x.cols[rank] : nullptr;
+  GemmArgs g{a, lda, b, ldb, bias, out_shard, ldo, M, n_local, K, b_is_nk ? 1 : 0,
              alpha, beta, dtype};
-  return launch_gemm_tc_allgather(g, x, s);
+  return launch_gemm_tc_allgather(g, x, out, s);
 }
 
 int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,
-                             const void* bias, void* const* outs, int64_t ldo, int64_t col0,
-                             int64_t M, int64_t N_local, int64_t K, int b_is_nk, float alpha,
+                             const void* bias, void* out, int64_t ldo, void* const* stages,
+                             const int64_t* cols, int64_t M, int64_t K, int b_is_nk, float alpha,
                              float beta, int dtype, const int* devices, int rank, int world,
                              uint32_t epoch, void* stream) {
   g_msg[0] = '\0';
@@ -347,7 +368,7 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
   cudaError_t e = cudaMemsetAsync(static_cast<uint32_t*>(flags[rank]) + kFlagCounter, 0,
                                   sizeof(uint32_t), s);
   if (e != cudaSuccess) return cuda_status(e, "clearing the static CTA counter");
-  return bi_gemm_allgather(a, lda, b, ldb, bias, outs, ldo, col0, M, N_local, K, b_is_nk, alpha,
+  return bi_gemm_allgather(a, lda, b, ldb, bias, out, ldo, stages, cols, M, K, b_is_nk, alpha,
                            beta, dtype, flags, rank, world, epoch, stream);
 }
 

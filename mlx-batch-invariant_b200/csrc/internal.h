@@ -22,11 +22,15 @@ struct GemmArgs {
   int dtype;
 };
 
-// Column-parallel GEMM with the all-gather fused into the epilogue.
+// Column-parallel GEMM with the all-gather fused into the epilogue.  Rank s owns the
+// global columns [cols[s], cols[s+1]).  Its finished tiles go to its own output
+// directly and, over NVLink, into every other rank's staging area as one dense
+// (M, cols[s+1] - cols[s]) row-major block at element offset M * cols[s]; each rank then
+// copies the blocks it received into its output (gather_unpack_kernel).
 struct GatherArgs {
-  void* outs[BI_MAX_PEERS];       // every rank's (M, ldo) output, mapped here
+  void* stages[BI_MAX_PEERS];     // every rank's staging area, mapped here
   uint32_t* flags[BI_MAX_PEERS];  // every rank's flag block, mapped here
-  int64_t col0;                   // first global column of this rank's shard
+  int64_t cols[BI_MAX_PEERS + 1]; // column partition: rank s owns [cols[s], cols[s+1])
   int rank, world;
   uint32_t epoch;
 };
@@ -66,7 +70,9 @@ constexpr int kSimtBN = 128;
 constexpr int kSimtBK = 8;
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
-int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, cudaStream_t stream);
+// g.out points at column cols[rank] of the output whose first column is out_base.
+int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, void* out_base,
+                             cudaStream_t stream);
 int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream);
 int static_flag_block(int device, void** out);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);

@@ -69,11 +69,15 @@ def _bind(lib):
     lib.bi_peer_barrier.restype = ctypes.c_int
     lib.bi_peer_barrier.argtypes = [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int,
                                     ctypes.c_uint32, _vp]
+    # (a, lda, b, ldb, bias, out, ldo, stages, cols, M, K, b_is_nk, alpha, beta, dtype,
+    #  flags | devices, rank, world, epoch, stream)
+    gather = [_vp, _i64, _vp, _i64, _vp, _vp, _i64, ctypes.POINTER(_vp), ctypes.POINTER(_i64),
+              _i64, _i64, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int]
+    tail = [ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _vp]
     lib.bi_gemm_allgather.restype = ctypes.c_int
-    lib.bi_gemm_allgather.argtypes = [_vp, _i64, _vp, _i64, _vp, ctypes.POINTER(_vp), _i64, _i64,
-                                      _i64, _i64, _i64, ctypes.c_int, ctypes.c_float,
-                                      ctypes.c_float, ctypes.c_int, ctypes.POINTER(_vp),
-                                      ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _vp]
+    lib.bi_gemm_allgather.argtypes = gather + [ctypes.POINTER(_vp)] + tail
+    lib.bi_gemm_allgather_static.restype = ctypes.c_int
+    lib.bi_gemm_allgather_static.argtypes = gather + [ctypes.POINTER(ctypes.c_int)] + tail
 
 
 def lib():

@@ -10,8 +10,10 @@ that sharding never adds a reduction and therefore never changes a bit:
   (pure data movement) assembles (M, N).  K-split or row-parallel plans are not
   offered: their cross-GPU sum would change the bits.
 * The all-gather can be fused into the GEMM (FusedColumnParallel): each rank's
-  epilogue stores its finished tiles straight into every rank's output over NVLink
-  peer mappings, so the exchange overlaps the math tile by tile.
+  epilogue stores its finished tiles into its own output and, over NVLink peer
+  mappings, into every other rank's staging area as one dense block, so the exchange
+  overlaps the math tile by tile; each rank then moves the received blocks into its
+  output with one local copy kernel.
 * Attention, head-parallel: rank r owns query heads [r*H/g, (r+1)*H/g) and the KV
   heads they read, [r*Hkv/g, (r+1)*Hkv/g) (Hkv % g == 0); each row is folded by one
   CTA exactly as on one GPU, and an all-gather over heads assembles the output.
@@ -143,41 +145,39 @@ def head_parallel_sdpa(q, k, v, *, scale=None, mask=None, sinks=None, group=None
     return gather_heads(y, group)
 
 
-class _DeviceBytes:
-    """__cuda_array_interface__ view of raw device bytes (no ownership)."""
-
-    def __init__(self, ptr, nbytes):
-        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (nbytes,),
-                                         "typestr": "|u1", "version": 3, "strides": None}
-
-
 class FusedColumnParallel:
     """Column-parallel ``linear`` over the ranks of `group` with the all-gather fused
     into the GEMM epilogue (libbi.so bi_gemm_allgather).
 
     Rank r holds rows shard_bounds(n_total, world)[r] of the (n_total, K) weight; every
     rank gets the full (..., n_total) output, bitwise equal to a single-GPU
-    ``linear``.  The output lives in a peer-mapped buffer of `max_rows` x `n_total`
-    elements owned by this object; ``linear`` returns a view of it that stays valid
-    until the next call (copy it to keep it).  All ranks must call ``linear`` and
-    ``close`` in the same order.  float16 / bfloat16 only (the tensor-core route).
+    ``linear``.  Each rank owns a peer-mapped staging area of `max_rows` x `n_total`
+    elements into which the other ranks store their shards as dense blocks; ``linear``
+    returns a new tensor (or fills `out`).  All ranks must call ``linear`` and
+    ``close`` in the same order.  float16 / bfloat16 only (the tensor-core route), and
+    n_total a multiple of 8 (every shard's block rows stay 16-byte aligned).
     """
 
     def __init__(self, n_total, max_rows, dtype, group=None):
         if dtype not in (torch.float16, torch.bfloat16):
             raise ValueError("the fused all-gather takes float16 or bfloat16")
+        if n_total % SHARD_ALIGN:
+            raise ValueError("the fused all-gather needs n_total %% %d == 0 (got %d)"
+                             % (SHARD_ALIGN, n_total))
         self.group = group
         self.world, self.rank = _group_info(group)
         if self.world > _lib.MAX_PEERS:
             raise ValueError("at most %d ranks" % _lib.MAX_PEERS)
         self.n_total, self.max_rows, self.dtype = n_total, max_rows, dtype
-        self.col0, self.col1 = shard_bounds(n_total, self.world)[self.rank]
+        bounds = shard_bounds(n_total, self.world)
+        self.col0, self.col1 = bounds[self.rank]
+        self._cols = (ctypes.c_int64 * (self.world + 1))(*([b[0] for b in bounds] + [n_total]))
         es = torch.empty((), dtype=dtype).element_size()
-        self._out_bytes = -(-max_rows * n_total * es // 256) * 256
+        self._stage_bytes = -(-max_rows * n_total * es // 256) * 256
         L = _lib.lib()
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        _lib.check(L.bi_peer_alloc(self._out_bytes + _lib.PEER_FLAG_BYTES, ctypes.byref(ptr),
+        _lib.check(L.bi_peer_alloc(self._stage_bytes + _lib.PEER_FLAG_BYTES, ctypes.byref(ptr),
                                    handle), "bi_peer_alloc")
         self._local = ptr.value
         handles = [None] * self.world
@@ -191,19 +191,17 @@ class FusedColumnParallel:
             _lib.check(L.bi_peer_open(h, ctypes.byref(q)), "bi_peer_open")
             self._ptrs.append(q.value)
             self._opened.append(q.value)
-        self._outs = (ctypes.c_void_p * self.world)(*self._ptrs)
-        self._flags = (ctypes.c_void_p * self.world)(*[p + self._out_bytes for p in self._ptrs])
+        self._stages = (ctypes.c_void_p * self.world)(*self._ptrs)
+        self._flags = (ctypes.c_void_p * self.world)(*[p + self._stage_bytes for p in self._ptrs])
         self._epoch = 0
-        dev = torch.cuda.current_device()
-        raw = torch.as_tensor(_DeviceBytes(self._local, self._out_bytes), device="cuda:%d" % dev)
-        self.buffer = raw.view(dtype)[:max_rows * n_total]
 
     @property
     def shard_rows(self):
         return self.col1 - self.col0
 
-    def linear(self, x, w_shard, bias_shard=None):
-        """y = x @ w.T (+ bias) on all ranks; w_shard is this rank's (shard, K) rows."""
+    def linear(self, x, w_shard, bias_shard=None, out=None):
+        """y = x @ w.T (+ bias) on all ranks; w_shard is this rank's (shard, K) rows.
+        `out`, if given, is a contiguous (..., n_total) tensor on x's device."""
         if x.dtype != self.dtype or w_shard.dtype != self.dtype:
             raise ValueError("x and w must be %s" % self.dtype)
         if w_shard.shape[0] != self.shard_rows:
@@ -214,9 +212,15 @@ class FusedColumnParallel:
         for d in lead:
             M *= d
         if M > self.max_rows:
-            raise ValueError("%d rows exceed the buffer's %d" % (M, self.max_rows))
+            raise ValueError("%d rows exceed the staging area's %d" % (M, self.max_rows))
         if w_shard.shape[0] and w_shard.shape[1] != K:
             raise ValueError("inner dimensions do not match: %d vs %d" % (K, w_shard.shape[1]))
+        if out is None:
+            out = torch.empty(*lead, self.n_total, dtype=self.dtype, device=x.device)
+        elif (out.shape != (*lead, self.n_total) or out.dtype != self.dtype
+              or out.device != x.device or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous %s tensor of shape %s on %s"
+                             % (self.dtype, (*lead, self.n_total), x.device))
         x2 = _aligned(x.reshape(M, K))
         w2 = _aligned(w_shard) if w_shard.shape[0] else w_shard
         b2 = bias_shard.to(self.dtype).contiguous() if bias_shard is not None else None
@@ -225,11 +229,11 @@ class FusedColumnParallel:
         with torch.cuda.device(dev):
             st = _lib.lib().bi_gemm_allgather(
                 x2.data_ptr(), K, w2.data_ptr() if w2.numel() else None, K,
-                b2.data_ptr() if b2 is not None else None, self._outs, self.n_total, self.col0,
-                M, self.shard_rows, K, 1, 1.0, 1.0, _lib.dtype_code(self.dtype), self._flags,
-                self.rank, self.world, self._epoch, _lib.stream_handle(dev))
+                b2.data_ptr() if b2 is not None else None, out.data_ptr(), self.n_total,
+                self._stages, self._cols, M, K, 1, 1.0, 1.0, _lib.dtype_code(self.dtype),
+                self._flags, self.rank, self.world, self._epoch, _lib.stream_handle(dev))
         _lib.check(st, "bi_gemm_allgather")
-        return self.buffer[:M * self.n_total].view(M, self.n_total).reshape(*lead, self.n_total)
+        return out
 
     def close(self):
         """Unmaps the peers' buffers and frees this one (collective)."""
@@ -243,6 +247,5 @@ class FusedColumnParallel:
         self._opened = []
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
-        self.buffer = None
         L.bi_peer_free(self._local)
         self._local = None

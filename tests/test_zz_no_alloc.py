@@ -18,19 +18,9 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _bind(L):
-    vp, i64 = ctypes.c_void_p, ctypes.c_int64
-    L.bi_gemm_allgather_static.restype = ctypes.c_int
-    L.bi_gemm_allgather_static.argtypes = [
-        vp, i64, vp, i64, vp, ctypes.POINTER(vp), i64, i64, i64, i64, i64, ctypes.c_int,
-        ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
-        ctypes.c_int, ctypes.c_int, ctypes.c_uint32, vp]
-
-
 def test_static_scratch_allgather_matches_the_allocating_entry_point():
     from mlx_batch_invariant_b200 import _lib
     L = _lib.lib()
-    _bind(L)
     dev = torch.cuda.current_device()
     stream = torch.cuda.current_stream().cuda_stream
     M, K, N = 300, 1024, 768
@@ -43,6 +33,10 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
                "bi_peer_alloc")
     flags = (ctypes.c_void_p * 1)(flag_ptr.value)
     devices = (ctypes.c_int * 1)(dev)
+    cols = (ctypes.c_int64 * 2)(0, N)
+    # one rank: no peer stores into the staging area, which must still be given
+    stage = torch.empty(M * N, dtype=torch.bfloat16, device="cuda")
+    stages = (ctypes.c_void_p * 1)(stage.data_ptr())
     try:
         for call in (1, 2):  # two calls in a row: the static block is reused
             x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
@@ -50,14 +44,13 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
             b = (torch.randn(N, generator=g) / 10).to(torch.bfloat16).cuda()
             want = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
             got = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
-            outs_want = (ctypes.c_void_p * 1)(want.data_ptr())
-            outs_got = (ctypes.c_void_p * 1)(got.data_ptr())
             _lib.check(L.bi_gemm_allgather(
-                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), outs_want, N, 0, M, N, K, 1,
-                1.0, 1.0, _lib.BI_BF16, flags, 0, 1, call, stream), "bi_gemm_allgather")
+                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), want.data_ptr(), N, stages, cols,
+                M, K, 1, 1.0, 1.0, _lib.BI_BF16, flags, 0, 1, call, stream), "bi_gemm_allgather")
             _lib.check(L.bi_gemm_allgather_static(
-                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), outs_got, N, 0, M, N, K, 1,
-                1.0, 1.0, _lib.BI_BF16, devices, 0, 1, call, stream), "bi_gemm_allgather_static")
+                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), got.data_ptr(), N, stages, cols,
+                M, K, 1, 1.0, 1.0, _lib.BI_BF16, devices, 0, 1, call, stream),
+                "bi_gemm_allgather_static")
             torch.cuda.synchronize()
             assert not torch.isnan(got).any(), "call %d left outputs unwritten" % call
             assert np.array_equal(got.view(torch.int16).cpu().numpy(),
@@ -71,10 +64,10 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
 def test_static_scratch_rejects_more_ranks_than_it_holds():
     from mlx_batch_invariant_b200 import _lib
     L = _lib.lib()
-    _bind(L)
     devices = (ctypes.c_int * 9)(*([torch.cuda.current_device()] * 9))
-    outs = (ctypes.c_void_p * 9)()
-    st = L.bi_gemm_allgather_static(None, 8, None, 8, None, outs, 8, 0, 1, 8, 8, 1, 1.0, 1.0,
-                                    _lib.BI_BF16, devices, 0, 9, 1, None)
+    stages = (ctypes.c_void_p * 9)()
+    cols = (ctypes.c_int64 * 10)(*range(0, 80, 8))
+    st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 72, stages, cols, 1, 8, 1,
+                                    1.0, 1.0, _lib.BI_BF16, devices, 0, 9, 1, None)
     assert st == -1
     assert b"at most 8 ranks" in L.bi_last_error()
