@@ -50,6 +50,9 @@ M = 4096
 DOMINANT = 2  # index of the (8192, 57344) GEMM in SHAPES
 SDPA_CFG = dict(B=64, H=32, Hkv=8, L=8192, D=128)
 FLOPS_PER_STEP = sum(2 * M * K * N for K, N in SHAPES)
+# NVLink 5 peer-copy bandwidth measured on these B200 nodes (GB/s per direction per GPU;
+# 900 nominal): the link term of the fused all-gather's roofline.
+LINK_GBS = 770.0
 
 
 # ---------------------------------------------------------------- helpers
@@ -351,6 +354,20 @@ def run_ours(args):
                 "kernel": "gemm_tc_kernel<bf16, (N,K)> M=%d K=%d N=%d" % (M, K, n_local),
                 "peak_source": "%s (%s)" % (peak_src,
                                             "sustained" if long_region else "burst")}
+    if world > 1:
+        # The fused call (entry barrier, GEMM whose epilogue stores this rank's shard
+        # into every peer, local unpack of the peers' blocks) is bound by the slower of
+        # the tensor work and the bytes this GPU must send over NVLink.
+        link_bytes = (world - 1) * M * n_local * 2
+        t_tensor = dom_flops / (peak * 1e12)
+        t_link = link_bytes / (LINK_GBS * 1e9)
+        target = max(t_tensor, t_link)
+        roofline["fused_allgather"] = {
+            "bound": "nvlink" if t_link > t_tensor else "tensor",
+            "nvlink_bytes_out": link_bytes, "link_gbs": LINK_GBS,
+            "link_peak_source": "measured peer copy, GB/s per direction per GPU",
+            "target_us": target * 1e6, "achieved_us": dom_ms * 1e3,
+            "frac": target / (dom_ms / 1e3)}
 
     # stock cuBLAS at the same shapes (the cost-of-invariance context)
     for _ in range(2):
