@@ -1,5 +1,6 @@
 """`python -m mlx_batch_invariant_b200 verify` -- prove on this machine that the
 kernels are batch-invariant (the B200 counterpart of mlx_batch_invariant/_cli.py).
+`... decoder` runs the same check end to end on a Llama-shaped model (decoder.py).
 
 Same sweep as the reference (_cli.py:78-152): for each dtype, bi.linear over batch
 sizes with a fixed row 0, and attention over query-chunk lengths with a fixed last
@@ -10,6 +11,7 @@ and head-parallel attention must give every rank the single-GPU bits.
 """
 
 import argparse
+import dataclasses
 import os
 import platform
 import sys
@@ -198,12 +200,136 @@ def verify(argv=None):
     return 1 if fails else 0
 
 
+SMALL_DECODER = dict(layers=2, hidden=1024, heads=16, kv_heads=8, head_dim=64, inter=2048,
+                     vocab=4096)
+
+
+def decoder(argv=None):
+    """The end-to-end check of the reference's bench/bench.py:211-246 (determinism) and
+    :161-208 (e2e) on the Llama-shaped decoder: the slot-0 logits of every prefill and
+    decode step at batch 1 and at --batch must be bitwise equal under the mode (and,
+    with --single-check under torchrun, equal to the unsharded model's); prints
+    tokens/s of both phases.  Stock torch is run as the control on one GPU."""
+    import json
+
+    from . import batch_invariant_mode
+    from . import decoder as dec
+
+    p = argparse.ArgumentParser(prog="python -m mlx_batch_invariant_b200 decoder")
+    p.add_argument("--layers", type=int, default=None, help="override the layer count")
+    p.add_argument("--small", action="store_true", help="a 2-layer d=1024 model")
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--gen", type=int, default=128)
+    p.add_argument("--exchange", choices=("fused", "nccl"), default="fused")
+    p.add_argument("--no-stock", action="store_true", help="skip the stock-torch control")
+    p.add_argument("--single-check", action="store_true",
+                   help="under torchrun: also run the unsharded model on every rank")
+    p.add_argument("--json", help="write the results here (rank 0)")
+    args = p.parse_args(argv)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        print("decoder needs a CUDA device (the kernels run on sm_100)", file=sys.stderr)
+        return 2
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    fields = dict(SMALL_DECODER) if args.small else {}
+    if args.layers is not None:
+        fields["layers"] = args.layers
+    cfg = dec.DecoderConfig(**fields)
+    say = print if rank == 0 else (lambda *a, **k: None)
+    max_len = args.prompt + args.gen
+    model = dec.Decoder(cfg, max_batch=args.batch, max_len=max_len, device=dev,
+                        exchange=args.exchange)
+    say("decoder: %d layers, d=%d, %d/%d heads x %d, ffn %d, vocab %d, %.2fB params, bf16, "
+        "%d GPU%s (%s exchange)" % (cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads,
+                                    cfg.head_dim, cfg.inter, cfg.vocab,
+                                    model.num_params() / 1e9, world, "s" if world > 1 else "",
+                                    args.exchange if world > 1 else "no"))
+    say("prompt %d tokens, then %d greedy decode steps; shared prompt in batch slot 0\n"
+        % (args.prompt, args.gen))
+
+    results = {"config": dataclasses.asdict(cfg), "gpus": world, "prompt": args.prompt,
+               "gen": args.gen, "exchange": args.exchange if world > 1 else None}
+    fails = 0
+    with batch_invariant_mode(strict=True):
+        runs = {}
+        for B in sorted({1, args.batch}):
+            stats, logits = dec.timed_run(model, B, args.prompt, args.gen, dev)
+            runs[B] = (stats, dec.slot0_bits(logits))
+    base = runs[1][1]
+    diff = dec.differing(runs[args.batch][1], base)
+    bad = sum(1 for d in diff if d)
+    fails += bad > 0
+    say("| path | batch | steps with slot-0 logits differing from batch 1 | logits differing |")
+    say("|---|---:|---:|---:|")
+    say("| batch invariant | %d | %d / %d | %d / %d |" % (args.batch, bad, len(diff), sum(diff),
+                                                        len(diff) * cfg.vocab))
+    results["invariant"] = {"batch": args.batch, "steps_differing": bad, "steps": len(diff),
+                            "logits_differing": sum(diff)}
+    if world == 1 and not args.no_stock:
+        stock = {}
+        for B in sorted({1, args.batch}):
+            _, logits = dec.timed_run(model, B, args.prompt, args.gen, dev, warm=False)
+            stock[B] = dec.slot0_bits(logits)
+        sd = dec.differing(stock[args.batch], stock[1])
+        say("| stock torch (control) | %d | %d / %d | %d / %d |"
+            % (args.batch, sum(1 for d in sd if d), len(sd), sum(sd), len(sd) * cfg.vocab))
+        results["stock"] = {"steps_differing": sum(1 for d in sd if d),
+                            "logits_differing": sum(sd)}
+    if world > 1 and args.single_check:
+        single = dec.Decoder(cfg, max_batch=1, max_len=max_len, device=dev, single=True)
+        with batch_invariant_mode(strict=True):
+            _, logits = dec.timed_run(single, 1, args.prompt, args.gen, dev, warm=False)
+        sc = dec.differing(dec.slot0_bits(logits), base)
+        ok = torch.tensor([int(any(sc))], device=dev)
+        dist.all_reduce(ok)
+        fails += int(ok.item()) > 0
+        say("| %d GPUs vs 1 GPU | 1 | %d ranks differ |" % (world, int(ok.item())))
+        results["vs_single_gpu_ranks_differing"] = int(ok.item())
+        del single
+
+    say("\n| phase | batch | tokens/s | seconds |")
+    say("|---|---:|---:|---:|")
+    for B in sorted(runs):
+        st = runs[B][0]
+        say("| prefill %d tok | %d | %.1f | %.4f |" % (args.prompt, B, st["prefill_tokens_per_s"],
+                                                    st["prefill_s"]))
+        if args.gen:
+            say("| decode %d steps | %d | %.1f | %.4f |" % (args.gen, B, st["decode_tokens_per_s"],
+                                                         st["decode_s"]))
+    results["runs"] = [runs[B][0] for B in sorted(runs)]
+    say("\n%s" % ("FAILED" if fails else "logits bitwise equal"))
+    if args.json and rank == 0:
+        with open(args.json, "w") as f:
+            json.dump(results, f, indent=1)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 1 if fails else 0
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     if argv and argv[0] == "verify":
         return verify(argv[1:])
+    if argv and argv[0] == "decoder":
+        return decoder(argv[1:])
     print("usage: python -m mlx_batch_invariant_b200 verify [--quick] "
-          "[--dtype float32|float16|bfloat16] [--seed N]", file=sys.stderr)
+          "[--dtype float32|float16|bfloat16] [--seed N]\n"
+          "       python -m mlx_batch_invariant_b200 decoder [--small] [--batch B] "
+          "[--prompt L] [--gen S] [--exchange fused|nccl] [--single-check]", file=sys.stderr)
     return 2
 
 

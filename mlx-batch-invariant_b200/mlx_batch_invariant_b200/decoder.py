@@ -1,0 +1,278 @@
+"""Llama-shaped decoder: the end-to-end invariance harness.
+
+The reference's harness (bench/bench.py:108-246: build_model, e2e, determinism) runs a
+random-init Llama-style decoder under batch_invariant_mode and checks that the logits
+of a prompt in batch slot 0 do not change when other prompts share the batch.  This is
+the same check on PyTorch CUDA tensors, with the shape of BASELINE config 4: 32 layers,
+d_model 4096, 32 query / 8 KV heads of 128, SwiGLU 14336, RMSNorm eps 1e-5, RoPE theta
+500000, vocab 128256, bf16 weights ~ N(0, 0.02); one prefill, then greedy decode steps
+against a static KV cache.
+
+On g GPUs (one process each, torch.distributed) every layer is column-parallel, so no
+value is ever summed across GPUs and the logits are also bitwise those of one GPU:
+
+* q/k/v: one fused weight per rank holding the rows of its query heads
+  [r*H/g, (r+1)*H/g) and KV heads [r*Hkv/g, (r+1)*Hkv/g); attention runs on the
+  rank's own heads against its own shard of the KV cache;
+* the attention output is all-gathered (pure data movement) before o_proj;
+* o_proj, down_proj and the LM head are column-parallel GEMMs whose output is
+  all-gathered -- fused into the GEMM epilogue (parallel.FusedColumnParallel) or,
+  with exchange="nccl", by a separate NCCL all-gather;
+* gate/up: rank r holds rows shard_bounds(inter, g)[r] of both, applies SwiGLU to its
+  slice and all-gathers the activation before down_proj.
+
+RMSNorm, SiLU, RoPE, the embedding lookup and the residual adds are stock PyTorch ops
+run on replicated rows; each computes every output element on its own, so they are
+batch-invariant on B200 (tests/test_mode_gpu.py guards that).
+"""
+
+import dataclasses
+import math
+import time
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import parallel
+from ._attention import scaled_dot_product_attention
+
+
+@dataclasses.dataclass(frozen=True)
+class DecoderConfig:
+    layers: int = 32
+    hidden: int = 4096
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    inter: int = 14336
+    vocab: int = 128256
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+    init_std: float = 0.02
+
+
+LLAMA_8B = DecoderConfig()
+
+
+def _weight(seed, rows, cols, std, device, dtype):
+    """A seeded (rows, cols) ~ N(0, std) weight, the same bits on every device."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    w = torch.randn((rows, cols), generator=g, device=device, dtype=torch.float32)
+    return (w * std).to(dtype)
+
+
+def _rope(t, cos, sin):
+    """Rotate-half RoPE in fp32 (each output element from its own inputs), rounded
+    back to t's dtype.  t (B, heads, L, hd); cos/sin (L, hd/2) fp32."""
+    h = t.shape[-1] // 2
+    x = t.float()
+    x1, x2 = x[..., :h], x[..., h:]
+    return torch.cat((x1 * cos - x2 * sin, x2 * cos + x1 * sin), dim=-1).to(t.dtype)
+
+
+class Decoder:
+    """Random-init Llama-style decoder with a static KV cache, sharded column-parallel
+    over the ranks of `group` (or unsharded with single=True / no process group).
+
+    prefill(ids) and decode(tok) return the logits of each row's last position,
+    (B, vocab), on every rank.  Run them inside batch_invariant_mode() for the
+    invariant path; outside it the local GEMMs and attention are stock PyTorch (the
+    control, and the CPU runs of the sharding plan).
+    """
+
+    def __init__(self, cfg=LLAMA_8B, max_batch=8, max_len=640, dtype=torch.bfloat16,
+                 device=None, seed=0, group=None, single=False, exchange="fused"):
+        if exchange not in ("fused", "nccl"):
+            raise ValueError("exchange must be 'fused' or 'nccl'")
+        self.cfg, self.dtype = cfg, dtype
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        distributed = dist.is_available() and dist.is_initialized() and not single
+        self.group = group
+        self.world = dist.get_world_size(group) if distributed else 1
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.exchange = exchange
+        H, Hkv, hd, d, inter = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.hidden, cfg.inter
+        g, r = self.world, self.rank
+        (h0, h1), (k0, k1) = parallel.head_shard(H, Hkv, r, g)
+        self.hq, self.hk = h1 - h0, k1 - k0
+        d0, d1 = parallel.shard_bounds(d, g)[r]
+        i0, i1 = parallel.shard_bounds(inter, g)[r]
+        v0, v1 = parallel.shard_bounds(cfg.vocab, g)[r]
+        self.inter_local = i1 - i0
+        dev, std = self.device, cfg.init_std
+
+        def w(seed_off, rows, cols, lo, hi):
+            full = _weight(seed * 1_000_003 + seed_off, rows, cols, std, dev, dtype)
+            part = full[lo:hi].contiguous()
+            del full
+            return part
+
+        self.layers = []
+        for layer in range(cfg.layers):
+            base = 16 * (layer + 1)
+            wq = w(base + 1, H * hd, d, h0 * hd, h1 * hd)
+            wk = w(base + 2, Hkv * hd, d, k0 * hd, k1 * hd)
+            wv = w(base + 3, Hkv * hd, d, k0 * hd, k1 * hd)
+            wg = w(base + 5, inter, d, i0, i1)
+            wu = w(base + 6, inter, d, i0, i1)
+            self.layers.append(dict(
+                wqkv=torch.cat((wq, wk, wv)).contiguous(),
+                wo=w(base + 4, d, H * hd, d0, d1),
+                wgu=torch.cat((wg, wu)).contiguous(),
+                wd=w(base + 7, d, inter, d0, d1),
+                n1=torch.ones(d, dtype=dtype, device=dev),
+                n2=torch.ones(d, dtype=dtype, device=dev)))
+            del wq, wk, wv, wg, wu
+        self.embed = w(1, cfg.vocab, d, 0, cfg.vocab)
+        self.norm = torch.ones(d, dtype=dtype, device=dev)
+        self.head = w(2, cfg.vocab, d, v0, v1)
+
+        self.max_batch, self.max_len = max_batch, max_len
+        shape = (max_batch, self.hk, max_len, hd)
+        self.cache_k = [torch.zeros(shape, dtype=dtype, device=dev) for _ in self.layers]
+        self.cache_v = [torch.zeros(shape, dtype=dtype, device=dev) for _ in self.layers]
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, device=dev,
+                                                     dtype=torch.float32) / hd))
+        ang = torch.arange(max_len, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
+        self.cos, self.sin = torch.cos(ang), torch.sin(ang)
+        self.pos = 0
+        self._fused = {}
+        if self.world > 1 and exchange == "fused":
+            rows = max_batch * max_len
+            self._fused[d] = parallel.FusedColumnParallel(d, rows, dtype, group)
+            self._fused["head"] = parallel.FusedColumnParallel(cfg.vocab, max_batch, dtype,
+                                                               group)
+
+    # ------------------------------------------------------------------ plumbing
+    def close(self):
+        """Releases the peer-mapped exchange buffers (collective when sharded)."""
+        for f in self._fused.values():
+            f.close()
+        self._fused = {}
+
+    def num_params(self):
+        c = self.cfg
+        per_layer = (c.heads + 2 * c.kv_heads) * c.head_dim * c.hidden \
+            + c.heads * c.head_dim * c.hidden + 3 * c.hidden * c.inter + 2 * c.hidden
+        return c.layers * per_layer + 2 * c.vocab * c.hidden + c.hidden
+
+    def _gather(self, t, n_total):
+        """(..., n_local) on every rank -> (..., n_total): the all-gather of a
+        column-parallel activation (shard_bounds layout)."""
+        if self.world == 1:
+            return t
+        lead = t.shape[:-1]
+        y = parallel.gather_columns(t.reshape(-1, t.shape[-1]), n_total, self.group)
+        return y.reshape(*lead, n_total)
+
+    def _column(self, x, w_shard, n_total, key):
+        """x @ w.T over the ranks (w sharded by rows), full output on every rank."""
+        if self.world > 1 and self.exchange == "fused":
+            return self._fused[key].linear(x, w_shard)
+        return self._gather(F.linear(x, w_shard), n_total)
+
+    def _attention(self, q, k, v, L):
+        from . import is_enabled
+        if is_enabled():
+            # bottom-right causal rule, right for chunked prefill too
+            return scaled_dot_product_attention(q, k, v, scale=1.0 / math.sqrt(q.shape[-1]),
+                                                mask="causal" if L > 1 else None)
+        if L > 1 and k.shape[2] != L:
+            raise NotImplementedError("the stock path prefills from position 0 only")
+        return F.scaled_dot_product_attention(q, k, v, is_causal=L > 1, enable_gqa=True)
+
+    # ------------------------------------------------------------------ forward
+    def _forward(self, ids):
+        cfg = self.cfg
+        B, L = ids.shape
+        if B > self.max_batch or self.pos + L > self.max_len:
+            raise ValueError("batch %d / length %d exceed the cache (%d, %d)"
+                             % (B, self.pos + L, self.max_batch, self.max_len))
+        d, hd, hq, hk = cfg.hidden, cfg.head_dim, self.hq, self.hk
+        p0 = self.pos
+        cos, sin = self.cos[p0:p0 + L], self.sin[p0:p0 + L]
+        x = F.embedding(ids, self.embed)
+        for li, p in enumerate(self.layers):
+            y = F.rms_norm(x, (d,), p["n1"], cfg.eps)
+            q, k, v = F.linear(y, p["wqkv"]).split((hq * hd, hk * hd, hk * hd), dim=-1)
+            q = _rope(q.reshape(B, L, hq, hd).transpose(1, 2), cos, sin)
+            k = _rope(k.reshape(B, L, hk, hd).transpose(1, 2), cos, sin)
+            self.cache_k[li][:B, :, p0:p0 + L] = k
+            self.cache_v[li][:B, :, p0:p0 + L] = v.reshape(B, L, hk, hd).transpose(1, 2)
+            n = p0 + L
+            a = self._attention(q, self.cache_k[li][:B, :, :n], self.cache_v[li][:B, :, :n], L)
+            a = self._gather(a.transpose(1, 2).reshape(B, L, hq * hd), cfg.heads * hd)
+            x = x + self._column(a, p["wo"], d, d)
+            y = F.rms_norm(x, (d,), p["n2"], cfg.eps)
+            gate, up = F.linear(y, p["wgu"]).split((self.inter_local, self.inter_local), dim=-1)
+            act = self._gather(F.silu(gate) * up, cfg.inter)
+            x = x + self._column(act, p["wd"], d, d)
+        self.pos += L
+        h = F.rms_norm(x[:, -1], (d,), self.norm, cfg.eps)
+        return self._column(h, self.head, cfg.vocab, "head")
+
+    def prefill(self, ids):
+        """Resets the cache and runs the prompt ids (B, L); logits (B, vocab)."""
+        self.pos = 0
+        return self._forward(ids)
+
+    def decode(self, tok):
+        """One step for tok (B,) or (B, 1); logits (B, vocab)."""
+        return self._forward(tok.reshape(-1, 1))
+
+
+def generate(model, ids, steps):
+    """Greedy: prefill, then `steps` decode steps.  Returns (list of (B, vocab) logits,
+    prefill seconds, decode seconds), timed on the device."""
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    logits = [model.prefill(ids)]
+    ev[1].record()
+    for _ in range(steps):
+        logits.append(model.decode(logits[-1].argmax(dim=-1)))
+    ev[2].record()
+    torch.cuda.synchronize()
+    return logits, ev[0].elapsed_time(ev[1]) / 1e3, ev[1].elapsed_time(ev[2]) / 1e3
+
+
+def prompts(cfg, batch, length, device, seed=7):
+    """The shared prompt in slot 0 and seeded random prompts in the other slots."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    shared = torch.randint(0, cfg.vocab, (1, length), generator=g, device=device)
+    others = torch.randint(0, cfg.vocab, (max(batch - 1, 0), length), generator=g,
+                           device=device)
+    return torch.cat((shared, others))[:batch]
+
+
+def slot0_bits(logits):
+    """The slot-0 rows of a generate() run, as raw 16-bit patterns (steps, vocab)."""
+    return torch.stack([t[0] for t in logits]).view(torch.int16)
+
+
+def differing(a, b):
+    """Per step: how many slot-0 logits differ between two slot0_bits tensors."""
+    return (a != b).sum(dim=-1).tolist()
+
+
+def timed_run(model, batch, prompt, steps, device, warm=True):
+    """tokens/s of prefill and decode at `batch` (after one untimed run)."""
+    ids = prompts(model.cfg, batch, prompt, device)
+    if warm:
+        generate(model, ids, min(steps, 4))
+    if model.world > 1:
+        dist.barrier(group=model.group)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    logits, tp, td = generate(model, ids, steps)
+    wall = time.perf_counter() - t0
+    if model.world > 1:
+        t = torch.tensor([tp, td], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=model.group)
+        tp, td = t.tolist()
+    return {"batch": batch, "prefill_tokens_per_s": batch * prompt / tp,
+            "decode_tokens_per_s": batch * steps / td if steps else None,
+            "prefill_s": tp, "decode_s": td, "wall_s": wall}, logits

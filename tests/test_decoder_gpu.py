@@ -1,0 +1,64 @@
+"""The Llama-shaped decoder harness on one GPU (the reference's bench/bench.py:211-246
+determinism check, extended over decode steps): under batch_invariant_mode the
+slot-0 logits of the prefill and of every greedy decode step are bitwise equal at
+batch 1, 3 and 8.  A 2-layer d=1024 model with the config's head layout keeps the
+test to seconds; the full 8B run is `python -m mlx_batch_invariant_b200 decoder`."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(layers=2, hidden=1024, heads=16, kv_heads=8, head_dim=64, inter=2048, vocab=4096)
+
+
+@pytest.fixture(scope="module")
+def model():
+    from mlx_batch_invariant_b200 import decoder as dec
+    m = dec.Decoder(dec.DecoderConfig(**SMALL), max_batch=8, max_len=48, device="cuda")
+    yield m
+    m.close()
+
+
+def _slot0(model, batch, prompt=37, steps=6):
+    from mlx_batch_invariant_b200 import decoder as dec
+    ids = dec.prompts(model.cfg, batch, prompt, "cuda")
+    logits, _, _ = dec.generate(model, ids, steps)
+    return dec.slot0_bits(logits)
+
+
+def test_decoder_logits_are_bitwise_equal_across_batch(model):
+    import mlx_batch_invariant_b200 as bi
+    from mlx_batch_invariant_b200 import decoder as dec
+    with bi.batch_invariant_mode(strict=True):
+        base = _slot0(model, 1)
+        for B in (3, 8):
+            assert dec.differing(_slot0(model, B), base) == [0] * base.shape[0], B
+
+
+def test_decoder_runs_the_invariant_kernels(model):
+    """The prefill's logits differ from stock torch's somewhere (the mode really
+    routed the GEMMs and attention), yet stay close to them."""
+    import mlx_batch_invariant_b200 as bi
+    from mlx_batch_invariant_b200 import decoder as dec
+    ids = dec.prompts(model.cfg, 2, 37, "cuda")
+    with bi.batch_invariant_mode(strict=True):
+        ours = model.prefill(ids).float()
+    stock = model.prefill(ids).float()
+    assert not torch.equal(ours, stock)
+    assert (ours - stock).abs().max().item() < 0.05 * stock.abs().max().item()
+
+
+def test_stock_rms_norm_is_row_invariant_at_prefill_sizes():
+    """F.rms_norm runs unwrapped in the decoder on (B, L, d) activations: a row's bits
+    must not depend on how many rows (up to a batch-8 x 512-token prefill) share it."""
+    d = 4096
+    g = torch.Generator(device="cuda").manual_seed(3)
+    w = torch.randn(d, generator=g, device="cuda").to(torch.bfloat16)
+    pool = torch.randn(4096, d, generator=g, device="cuda").to(torch.bfloat16)
+    row = pool[:1].clone()
+    want = torch.nn.functional.rms_norm(row, (d,), w, 1e-5).view(torch.int16)
+    for rows, shape in ((512, (1, 512, d)), (4096, (8, 512, d)), (3, (3, 1, d))):
+        x = pool[:rows].clone().reshape(shape)
+        y = torch.nn.functional.rms_norm(x, (d,), w, 1e-5).reshape(rows, d)
+        assert torch.equal(y[:1].view(torch.int16), want), rows

@@ -194,3 +194,57 @@ def test_a_rank_that_dies_makes_the_other_fail_not_hang():
     results = _spawn(_dying_worker, timeout=90)
     assert results[1] == "exiting"
     assert results[0].startswith("raised"), results[0]
+
+
+TINY_DECODER = dict(layers=2, hidden=64, heads=4, kv_heads=2, head_dim=16, inter=96, vocab=128)
+
+
+def _greedy(model, ids, steps):
+    out = [model.prefill(ids)]
+    for _ in range(steps):
+        out.append(model.decode(out[-1].argmax(dim=-1)))
+    return torch.stack(out)
+
+
+def _decoder_worker(rank, world, port, queue):
+    _setup_paths()
+    import torch.distributed as dist
+    from mlx_batch_invariant_b200 import decoder as dec
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    cfg = dec.DecoderConfig(**TINY_DECODER)
+    model = dec.Decoder(cfg, max_batch=2, max_len=12, dtype=torch.float32, device="cpu",
+                        exchange="nccl")
+    shards = {"wqkv": model.layers[1]["wqkv"].clone(), "wd": model.layers[1]["wd"].clone()}
+    logits = _greedy(model, dec.prompts(cfg, 2, 6, "cpu"), 4)
+    queue.put((rank, {"logits": logits.numpy(), **{k: v.numpy() for k, v in shards.items()}}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_decoder_sharding_plan_matches_one_process():
+    """The decoder's column-parallel plan on 2 gloo ranks (stock float32 ops on CPU):
+    each rank holds the right rows of every weight and ends with the logits and greedy
+    tokens of the unsharded model.  (Bitwise equality across GPU counts is the GPU
+    test's job; CPU BLAS gives no per-element guarantee across shard widths.)"""
+    _setup_paths()
+    from mlx_batch_invariant_b200 import decoder as dec
+    results = _spawn(_decoder_worker)
+    cfg = dec.DecoderConfig(**TINY_DECODER)
+    single = dec.Decoder(cfg, max_batch=2, max_len=12, dtype=torch.float32, device="cpu",
+                         single=True)
+    want = _greedy(single, dec.prompts(cfg, 2, 6, "cpu"), 4).numpy()
+    hd, H, Hkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+    wqkv = single.layers[1]["wqkv"].numpy()
+    q, k, v = np.split(wqkv, [H * hd, (H + Hkv) * hd])
+    for r in (0, 1):
+        got = results[r]
+        np.testing.assert_allclose(got["logits"], want, rtol=1e-4, atol=1e-5)
+        assert np.array_equal(got["logits"].argmax(-1), want.argmax(-1))
+        hq, hk = H // 2 * hd, Hkv // 2 * hd
+        np.testing.assert_array_equal(got["wqkv"], np.concatenate(
+            (q[r * hq:(r + 1) * hq], k[r * hk:(r + 1) * hk], v[r * hk:(r + 1) * hk])))
+        half = cfg.hidden // 2
+        np.testing.assert_array_equal(got["wd"], single.layers[1]["wd"].numpy()[r * half:(r + 1) * half])
