@@ -151,7 +151,13 @@ int bi_peer_free(void* ptr);
 
 /* Stream-ordered barrier over `world` ranks: rank `rank` posts `epoch` to every
  * rank's flag block and waits (bounded) until every rank has posted it to its own.
- * flags[r] is rank r's flag block (BI_PEER_FLAG_BYTES), mapped in this process. */
+ * flags[r] is rank r's flag block (BI_PEER_FLAG_BYTES), mapped in this process.
+ *
+ * Epochs (here and in bi_gemm_allgather*): either every call on a flag block passes
+ * a value larger than any earlier call's, or every call passes 0 and the block counts
+ * its calls itself (a word in the block, advanced on the device by each call's entry
+ * barrier).  Use 0 for calls captured in a CUDA graph, whose replays repeat their
+ * arguments.  Ranks must make the same calls in the same order either way. */
 int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, void* stream);
 
 /*
@@ -166,7 +172,8 @@ int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, voi
  *              M * cols[world] elements; rank s writes its block (M, N_s) row-major at
  *              element offset M * cols[s] of every other rank's area.
  *   cols       world + 1 column bounds: cols[0] = 0, nondecreasing, multiples of 8.
- *   flags[r]   rank r's flag block.  epoch: a value larger than any earlier call's.
+ *   flags[r]   rank r's flag block.  epoch: see bi_peer_barrier (0 = counted on the
+ *              device, for graph capture).
  * On return (stream order) `out` holds all cols[world] columns.  Calls an entry barrier
  * first, so no peer writes a staging area its owner may still read.  Same arithmetic,
  * tile and route rules as bi_gemm.
@@ -203,7 +210,8 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
  * device current (cudaGetSymbolAddress) and caches the address; make that first call
  * before any stream capture.  All calls on a device share its block, which keeps the
  * last call's contents: each call clears the block's CTA counter on `stream` before
- * use, and `epoch` must exceed the epoch of every earlier call on the same devices.
+ * use, and `epoch` must exceed the epoch of every earlier call on the same devices (or
+ * be 0 on every call: the block then counts the calls itself).
  * Calls whose work overlaps on the GPU (different streams, or different rank groups
  * sharing a device) race on the block.
  */

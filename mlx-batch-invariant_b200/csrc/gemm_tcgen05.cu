@@ -57,23 +57,43 @@ constexpr int BM = kTcBM;    // rows per CTA (the pair covers 2*BM)
 constexpr int BN = kTcBN;    // columns per pair tile
 constexpr int BN_CTA = BN / 2;  // B columns each CTA loads
 constexpr int BK = kTcBK;    // 64 x 2 bytes = one 128-byte swizzle row
-constexpr int STAGES = 6;
 constexpr int UMMA_K = 16;
-constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KiB
 constexpr int B_STAGE_BYTES = BN_CTA * BK * 2;  // 16 KiB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int ACC_BUFS = 2;
 constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512: the whole tensor memory of the SM
 constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARPS = 4;
-constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
 // Epilogue staging: each epilogue warp turns 32 rows x 128 columns of finished outputs
 // around in shared memory so a store instruction writes 256 contiguous bytes of a row.
 constexpr int EPI_COLS = 128;
 constexpr int EPI_STAGE_BYTES = 32 * EPI_COLS * 2;  // per warp, 16-bit outputs
-constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES +
-                           EPI_WARPS * EPI_STAGE_BYTES + NUM_BARRIERS * 8 + 16;
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory above the per-CTA limit");
+
+// The shared-memory ring that feeds the UMMAs.  It decides how many rows of A each
+// stage holds and how many stages are in flight -- never the tile, the instruction or
+// the K order.
+//   WideRing  every CTA loads its 128 rows of A; 6 stages of 16 + 16 KiB.
+//   ThinRing  M <= 16: only rows 0-15 of the pair tile exist, so CTA 0 loads a
+//             16-row A box and CTA 1 none; the freed memory holds 10 stages, keeping
+//             160 KiB of W in flight per SM (decode is bound by streaming W).
+//             The UMMA still reads 128 rows per CTA: rows past the box hold whatever
+//             the shared memory held, which only reaches output rows >= 16 (>= M),
+//             and those are never stored.
+template <int A_ROWS_, int STAGES_>
+struct RingCfg {
+  static constexpr int A_ROWS = A_ROWS_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr bool THIN = A_ROWS_ < BM;
+  static constexpr int A_STAGE_BYTES = A_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+  static constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
+  static constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES +
+                                    EPI_WARPS * EPI_STAGE_BYTES + NUM_BARRIERS * 8 + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory above the per-CTA limit");
+  static_assert(A_STAGE_BYTES % 1024 == 0, "A stages must keep 1 KiB swizzle alignment");
+};
+using WideRing = RingCfg<BM, 6>;
+using ThinRing = RingCfg<16, 10>;
+constexpr int THIN_MAX_M = ThinRing::A_ROWS;
 constexpr int GROUP_M = 8;  // pair-tiles of M that consecutive tile indices sweep (L2 reuse)
 constexpr uint16_t PAIR_MASK = 0x3;
 
@@ -110,10 +130,21 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   tn = in_group / rows;
 }
 
-template <typename T, bool B_NK, bool GATHER>
+// The epoch of the current call: the explicit one, or (epoch 0) the count the call's
+// entry barrier stored in the local flag block.
+__device__ __forceinline__ uint32_t call_epoch(const GatherArgs& x) {
+  return x.epoch != 0 ? x.epoch
+                      : *reinterpret_cast<volatile uint32_t*>(x.flags[x.rank] + kFlagEpoch);
+}
+
+template <typename T, bool B_NK, bool GATHER, typename R>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  constexpr int STAGES = R::STAGES;
+  constexpr int A_STAGE_BYTES = R::A_STAGE_BYTES;
+  constexpr int STAGE_BYTES = R::STAGE_BYTES;
+  constexpr int NUM_BARRIERS = R::NUM_BARRIERS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -180,10 +211,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+          // the leader's barrier counts both CTAs' bytes (a thin ring: one A box)
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage],
+                                  (R::THIN ? 1 : 2) * A_STAGE_BYTES + 2 * B_STAGE_BYTES);
+          }
           const uint32_t bar = full_leader0 + stage * 8;
-          tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tmap_a, bar, kb * BK,
-                           tm * 2 * BM + static_cast<int>(rank) * BM);
+          if (!R::THIN || leader) {
+            tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tmap_a, bar, kb * BK,
+                             tm * 2 * BM + static_cast<int>(rank) * BM);
+          }
           uint8_t* dstB = sB + stage * B_STAGE_BYTES;
           const int n0 = tn * BN + static_cast<int>(rank) * BN_CTA;
           if (B_NK) {
@@ -443,11 +480,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (atomicAdd(counter, 1u) == gridDim.x - 1) {
         *counter = 0;  // the next call's CTAs start from zero (stream order)
         __threadfence_system();
+        const uint32_t epoch = call_epoch(p.gx);
         for (int r = 0; r < p.gx.world; ++r) {
-          st_release_sys(p.gx.flags[r] + kFlagExit + p.gx.rank, p.gx.epoch);
+          st_release_sys(p.gx.flags[r] + kFlagExit + p.gx.rank, epoch);
         }
         for (int r = 0; r < p.gx.world; ++r) {
-          if (!wait_flag_at_least(p.gx.flags[p.gx.rank] + kFlagExit + r, p.gx.epoch)) {
+          if (!wait_flag_at_least(p.gx.flags[p.gx.rank] + kFlagExit + r, epoch)) {
             record_error(&g_error_word, (kSitePeerExit << 8) | kErrReasonTimeout);
             break;
           }
@@ -502,17 +540,28 @@ __global__ void __launch_bounds__(UNPACK_THREADS)
 
 // Stream-ordered barrier over the ranks of a GatherArgs (one warp): post the epoch to
 // every rank's flag `slot` (entry or exit), then wait (bounded) for every rank's.
+// With x.epoch == 0 the entry barrier takes the block's call count + 1 as the epoch
+// and stores it back afterwards, so the call's later kernels (call_epoch) and the
+// next call see it; ranks that make the same calls keep equal counts.
 __global__ void peer_barrier_kernel(const GatherArgs x, int slot) {
   const int t = threadIdx.x;
+  uint32_t* own = x.flags[x.rank];
+  uint32_t epoch = x.epoch;
+  if (epoch == 0) {
+    epoch = *reinterpret_cast<volatile uint32_t*>(own + kFlagEpoch);
+    if (slot == kFlagEntry) epoch += 1;
+  }
   __threadfence_system();
-  if (t < x.world) st_release_sys(x.flags[t] + slot + x.rank, x.epoch);
+  if (t < x.world) st_release_sys(x.flags[t] + slot + x.rank, epoch);
   __syncwarp();
   bool ok = true;
-  if (t < x.world) ok = wait_flag_at_least(x.flags[x.rank] + slot + t, x.epoch);
+  if (t < x.world) ok = wait_flag_at_least(own + slot + t, epoch);
   if (!ok) {
     record_error(&g_error_word,
                  ((slot == kFlagEntry ? kSitePeerEntry : kSitePeerExit) << 8) | kErrReasonTimeout);
   }
+  __syncwarp();
+  if (x.epoch == 0 && slot == kFlagEntry && t == 0) own[kFlagEpoch] = epoch;
 }
 
 // ---------------------------------------------------------------------------
@@ -561,10 +610,10 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
   return BI_OK;
 }
 
-template <typename T, bool B_NK, bool GATHER>
-static int launch_typed(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
+template <typename T, bool B_NK, bool GATHER, typename R>
+static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
   CUtensorMap ma, mb;
-  int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, BM, g.dtype);
+  int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, R::A_ROWS, g.dtype);
   if (st) return st;
   if (B_NK) {
     st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, BN_CTA, g.dtype);
@@ -573,10 +622,10 @@ static int launch_typed(const GemmArgs& g, const GatherArgs* gx, cudaStream_t st
   }
   if (st) return st;
 
-  auto kern = gemm_tc_kernel<T, B_NK, GATHER>;
+  auto kern = gemm_tc_kernel<T, B_NK, GATHER, R>;
   // The attribute is per device; setting it again is cheap and capture-safe.
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES);
+                                       R::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_tc)");
 
   Params p;
@@ -599,8 +648,16 @@ static int launch_typed(const GemmArgs& g, const GatherArgs* gx, cudaStream_t st
   }
   const int max_pairs = device_sm_count() / 2;
   const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
-  kern<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  kern<<<2 * pairs, NUM_THREADS, R::SMEM_BYTES, stream>>>(ma, mb, p);
   return cuda_status(cudaGetLastError(), "gemm_tc launch");
+}
+
+// The ring is the only thing M selects: a thin one when every row of the problem fits
+// in the 16-row A box (decode), else the wide one.  Both run the same UMMAs.
+template <typename T, bool B_NK, bool GATHER>
+static int launch_typed(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
+  return g.M <= THIN_MAX_M ? launch_ring<T, B_NK, GATHER, ThinRing>(g, gx, stream)
+                           : launch_ring<T, B_NK, GATHER, WideRing>(g, gx, stream);
 }
 
 template <bool GATHER>

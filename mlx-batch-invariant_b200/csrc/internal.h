@@ -36,10 +36,12 @@ struct GatherArgs {
 };
 
 // Flag block layout (32-bit words): [0, 8) exit flags posted by rank r, [8, 16) entry
-// flags posted by rank r, [16] CTA-completion counter of the local GEMM.
+// flags posted by rank r, [16] CTA-completion counter of the local GEMM, [17] the
+// block's own call count (the epoch of calls made with epoch 0).
 constexpr int kFlagExit = 0;
 constexpr int kFlagEntry = BI_MAX_PEERS;
 constexpr int kFlagCounter = 2 * BI_MAX_PEERS;
+constexpr int kFlagEpoch = 2 * BI_MAX_PEERS + 1;
 
 struct SdpaArgs {
   const void* q;

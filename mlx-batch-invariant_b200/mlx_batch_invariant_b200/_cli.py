@@ -223,6 +223,8 @@ def decoder(argv=None):
     p.add_argument("--gen", type=int, default=128)
     p.add_argument("--exchange", choices=("fused", "nccl"), default="fused")
     p.add_argument("--no-stock", action="store_true", help="skip the stock-torch control")
+    p.add_argument("--eager", action="store_true",
+                   help="decode step by step from Python instead of replaying a CUDA graph")
     p.add_argument("--single-check", action="store_true",
                    help="under torchrun: also run the unsharded model on every rank")
     p.add_argument("--json", help="write the results here (rank 0)")
@@ -256,17 +258,24 @@ def decoder(argv=None):
                                     cfg.head_dim, cfg.inter, cfg.vocab,
                                     model.num_params() / 1e9, world, "s" if world > 1 else "",
                                     args.exchange if world > 1 else "no"))
-    say("prompt %d tokens, then %d greedy decode steps; shared prompt in batch slot 0\n"
-        % (args.prompt, args.gen))
+    say("prompt %d tokens, then %d greedy decode steps (%s); shared prompt in batch slot 0\n"
+        % (args.prompt, args.gen, "eager" if args.eager else "CUDA graph replays"))
+
+    def run(B, warm=True):
+        graph = dec.DecodeGraph(model, B) if args.gen and not args.eager else None
+        stats, logits = dec.timed_run(model, B, args.prompt, args.gen, dev, warm=warm,
+                                      graph=graph)
+        del graph  # a graph holding NCCL calls must go before the process group
+        return stats, dec.slot0_bits(logits)
 
     results = {"config": dataclasses.asdict(cfg), "gpus": world, "prompt": args.prompt,
-               "gen": args.gen, "exchange": args.exchange if world > 1 else None}
+               "gen": args.gen, "exchange": args.exchange if world > 1 else None,
+               "decode": "eager" if args.eager else "cuda graph"}
     fails = 0
     with batch_invariant_mode(strict=True):
         runs = {}
         for B in sorted({1, args.batch}):
-            stats, logits = dec.timed_run(model, B, args.prompt, args.gen, dev)
-            runs[B] = (stats, dec.slot0_bits(logits))
+            runs[B] = run(B)
     base = runs[1][1]
     diff = dec.differing(runs[args.batch][1], base)
     bad = sum(1 for d in diff if d)
@@ -280,8 +289,7 @@ def decoder(argv=None):
     if world == 1 and not args.no_stock:
         stock = {}
         for B in sorted({1, args.batch}):
-            _, logits = dec.timed_run(model, B, args.prompt, args.gen, dev, warm=False)
-            stock[B] = dec.slot0_bits(logits)
+            stock[B] = run(B, warm=False)[1]
         sd = dec.differing(stock[args.batch], stock[1])
         say("| stock torch (control) | %d | %d / %d | %d / %d |"
             % (args.batch, sum(1 for d in sd if d), len(sd), sum(sd), len(sd) * cfg.vocab))

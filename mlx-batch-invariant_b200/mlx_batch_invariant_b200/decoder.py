@@ -138,6 +138,7 @@ class Decoder:
                                                      dtype=torch.float32) / hd))
         ang = torch.arange(max_len, device=dev, dtype=torch.float32)[:, None] * inv[None, :]
         self.cos, self.sin = torch.cos(ang), torch.sin(ang)
+        self._key_pos = torch.arange(max_len, device=dev)
         self.pos = 0
         self._fused = {}
         if self.world > 1 and exchange == "fused":
@@ -174,43 +175,66 @@ class Decoder:
             return self._fused[key].linear(x, w_shard)
         return self._gather(F.linear(x, w_shard), n_total)
 
-    def _attention(self, q, k, v, L):
+    def _attention(self, q, k, v, L, mask=None):
         from . import is_enabled
         if is_enabled():
             # bottom-right causal rule, right for chunked prefill too
+            m = mask if mask is not None else ("causal" if L > 1 else None)
             return scaled_dot_product_attention(q, k, v, scale=1.0 / math.sqrt(q.shape[-1]),
-                                                mask="causal" if L > 1 else None)
+                                                mask=m)
+        if mask is not None:
+            return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True)
         if L > 1 and k.shape[2] != L:
             raise NotImplementedError("the stock path prefills from position 0 only")
         return F.scaled_dot_product_attention(q, k, v, is_causal=L > 1, enable_gqa=True)
 
     # ------------------------------------------------------------------ forward
-    def _forward(self, ids):
+    def _forward(self, ids, pos=None):
+        """Logits of each row's last position.  pos None: the host position self.pos
+        (prefill or an eager decode step).  pos a (1,) device tensor: one decode step
+        whose position is read on the device -- RoPE rows by index_select, the cache
+        write by index_copy_, and attention over the whole cache with the keys after
+        the position masked out (a masked key is skipped, so the logits are those of
+        the eager step) -- the form a CUDA graph can replay at every position."""
         cfg = self.cfg
         B, L = ids.shape
-        if B > self.max_batch or self.pos + L > self.max_len:
-            raise ValueError("batch %d / length %d exceed the cache (%d, %d)"
+        static = pos is not None
+        if B > self.max_batch or (static and L != 1) or (
+                not static and self.pos + L > self.max_len):
+            raise ValueError("batch %d / length %d do not fit the cache (%d, %d)"
                              % (B, self.pos + L, self.max_batch, self.max_len))
         d, hd, hq, hk = cfg.hidden, cfg.head_dim, self.hq, self.hk
-        p0 = self.pos
-        cos, sin = self.cos[p0:p0 + L], self.sin[p0:p0 + L]
+        if static:
+            cos, sin = self.cos.index_select(0, pos), self.sin.index_select(0, pos)
+            mask = torch.where(self._key_pos <= pos, 0.0, float("-inf")).to(self.dtype)
+            mask = mask.view(1, 1, 1, self.max_len)
+        else:
+            p0, mask = self.pos, None
+            cos, sin = self.cos[p0:p0 + L], self.sin[p0:p0 + L]
         x = F.embedding(ids, self.embed)
         for li, p in enumerate(self.layers):
             y = F.rms_norm(x, (d,), p["n1"], cfg.eps)
             q, k, v = F.linear(y, p["wqkv"]).split((hq * hd, hk * hd, hk * hd), dim=-1)
             q = _rope(q.reshape(B, L, hq, hd).transpose(1, 2), cos, sin)
             k = _rope(k.reshape(B, L, hk, hd).transpose(1, 2), cos, sin)
-            self.cache_k[li][:B, :, p0:p0 + L] = k
-            self.cache_v[li][:B, :, p0:p0 + L] = v.reshape(B, L, hk, hd).transpose(1, 2)
-            n = p0 + L
-            a = self._attention(q, self.cache_k[li][:B, :, :n], self.cache_v[li][:B, :, :n], L)
+            v = v.reshape(B, L, hk, hd).transpose(1, 2)
+            ck, cv = self.cache_k[li][:B], self.cache_v[li][:B]
+            if static:
+                ck.index_copy_(2, pos, k)
+                cv.index_copy_(2, pos, v)
+                a = self._attention(q, ck, cv, 1, mask)
+            else:
+                ck[:, :, p0:p0 + L] = k
+                cv[:, :, p0:p0 + L] = v
+                a = self._attention(q, ck[:, :, :p0 + L], cv[:, :, :p0 + L], L)
             a = self._gather(a.transpose(1, 2).reshape(B, L, hq * hd), cfg.heads * hd)
             x = x + self._column(a, p["wo"], d, d)
             y = F.rms_norm(x, (d,), p["n2"], cfg.eps)
             gate, up = F.linear(y, p["wgu"]).split((self.inter_local, self.inter_local), dim=-1)
             act = self._gather(F.silu(gate) * up, cfg.inter)
             x = x + self._column(act, p["wd"], d, d)
-        self.pos += L
+        if not static:
+            self.pos += L
         h = F.rms_norm(x[:, -1], (d,), self.norm, cfg.eps)
         return self._column(h, self.head, cfg.vocab, "head")
 
@@ -220,19 +244,68 @@ class Decoder:
         return self._forward(ids)
 
     def decode(self, tok):
-        """One step for tok (B,) or (B, 1); logits (B, vocab)."""
+        """One eager step for tok (B,) or (B, 1); logits (B, vocab)."""
         return self._forward(tok.reshape(-1, 1))
 
+    def _greedy_step(self, tok, pos):
+        """The static decode step: logits for tok (B, 1) at device position pos, then
+        tok <- argmax and pos <- pos + 1, all on the device."""
+        logits = self._forward(tok, pos)
+        tok.copy_(logits.argmax(dim=-1, keepdim=True))
+        pos.add_(1)
+        return logits
 
-def generate(model, ids, steps):
-    """Greedy: prefill, then `steps` decode steps.  Returns (list of (B, vocab) logits,
-    prefill seconds, decode seconds), timed on the device."""
+
+class DecodeGraph:
+    """One greedy decode step at a fixed batch, captured once in a CUDA graph and
+    replayed for every position (the token and position live in device buffers that
+    the step itself advances).  Capture inside batch_invariant_mode to record the
+    invariant kernels; replays need no mode.  Sharded models capture their NCCL and
+    fused all-gathers too (the fused exchange counts its epochs on the device)."""
+
+    def __init__(self, model, batch):
+        self.model, self.batch = model, batch
+        dev = model.device
+        self.tok = torch.zeros((batch, 1), dtype=torch.long, device=dev)
+        # the warm-up writes the last cache slot, which every later step at that
+        # position rewrites before reading it
+        self.pos = torch.full((1,), model.max_len - 1, dtype=torch.long, device=dev)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            model._greedy_step(self.tok, self.pos)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.pos.fill_(model.max_len - 1)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = model._greedy_step(self.tok, self.pos)
+
+    def start(self, tok, pos):
+        """Continue from host position `pos` with tokens tok (B,) (device tensors)."""
+        self.tok.copy_(tok.reshape(self.batch, 1))
+        self.pos.fill_(pos)
+
+    def step(self):
+        """One decode step; returns the graph's logits buffer (overwritten by the next)."""
+        self.graph.replay()
+        return self.logits
+
+
+def generate(model, ids, steps, graph=None):
+    """Greedy: prefill, then `steps` decode steps (replays of `graph`, a DecodeGraph of
+    this batch, if given).  Returns (list of (B, vocab) logits, prefill seconds, decode
+    seconds), timed on the device."""
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     ev[0].record()
     logits = [model.prefill(ids)]
     ev[1].record()
-    for _ in range(steps):
-        logits.append(model.decode(logits[-1].argmax(dim=-1)))
+    if graph is not None:
+        graph.start(logits[0].argmax(dim=-1), model.pos)
+        for _ in range(steps):
+            logits.append(graph.step().clone())
+    else:
+        for _ in range(steps):
+            logits.append(model.decode(logits[-1].argmax(dim=-1)))
     ev[2].record()
     torch.cuda.synchronize()
     return logits, ev[0].elapsed_time(ev[1]) / 1e3, ev[1].elapsed_time(ev[2]) / 1e3
@@ -258,16 +331,16 @@ def differing(a, b):
     return (a != b).sum(dim=-1).tolist()
 
 
-def timed_run(model, batch, prompt, steps, device, warm=True):
+def timed_run(model, batch, prompt, steps, device, warm=True, graph=None):
     """tokens/s of prefill and decode at `batch` (after one untimed run)."""
     ids = prompts(model.cfg, batch, prompt, device)
     if warm:
-        generate(model, ids, min(steps, 4))
+        generate(model, ids, min(steps, 4), graph)
     if model.world > 1:
         dist.barrier(group=model.group)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    logits, tp, td = generate(model, ids, steps)
+    logits, tp, td = generate(model, ids, steps, graph)
     wall = time.perf_counter() - t0
     if model.world > 1:
         t = torch.tensor([tp, td], dtype=torch.float64, device=device)

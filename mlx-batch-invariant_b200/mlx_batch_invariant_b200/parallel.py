@@ -154,7 +154,8 @@ class FusedColumnParallel:
     ``linear``.  Each rank owns a peer-mapped staging area of `max_rows` x `n_total`
     elements into which the other ranks store their shards as dense blocks; ``linear``
     returns a new tensor (or fills `out`).  All ranks must call ``linear`` and
-    ``close`` in the same order.  float16 / bfloat16 only (the tensor-core route), and
+    ``close`` in the same order.  The flag block counts the calls on the device (epoch
+    0), so ``linear`` may be captured in a CUDA graph and replayed.  float16 / bfloat16 only (the tensor-core route), and
     n_total a multiple of 8 (every shard's block rows stay 16-byte aligned).
     """
 
@@ -193,7 +194,6 @@ class FusedColumnParallel:
             self._opened.append(q.value)
         self._stages = (ctypes.c_void_p * self.world)(*self._ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*[p + self._stage_bytes for p in self._ptrs])
-        self._epoch = 0
 
     @property
     def shard_rows(self):
@@ -224,14 +224,13 @@ class FusedColumnParallel:
         x2 = _aligned(x.reshape(M, K))
         w2 = _aligned(w_shard) if w_shard.shape[0] else w_shard
         b2 = bias_shard.to(self.dtype).contiguous() if bias_shard is not None else None
-        self._epoch = (self._epoch + 1) & 0xFFFFFFFF or 1
         dev = x.device
         with torch.cuda.device(dev):
             st = _lib.lib().bi_gemm_allgather(
                 x2.data_ptr(), K, w2.data_ptr() if w2.numel() else None, K,
                 b2.data_ptr() if b2 is not None else None, out.data_ptr(), self.n_total,
                 self._stages, self._cols, M, K, 1, 1.0, 1.0, _lib.dtype_code(self.dtype),
-                self._flags, self.rank, self.world, self._epoch, _lib.stream_handle(dev))
+                self._flags, self.rank, self.world, 0, _lib.stream_handle(dev))
         _lib.check(st, "bi_gemm_allgather")
         return out
 

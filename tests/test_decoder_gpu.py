@@ -62,3 +62,19 @@ def test_stock_rms_norm_is_row_invariant_at_prefill_sizes():
         x = pool[:rows].clone().reshape(shape)
         y = torch.nn.functional.rms_norm(x, (d,), w, 1e-5).reshape(rows, d)
         assert torch.equal(y[:1].view(torch.int16), want), rows
+
+
+def test_graph_decode_matches_eager_decode_bitwise(model):
+    """DecodeGraph replays (device position, full-cache attention with the later keys
+    masked out) give the eager decode's bits, and stay batch-invariant."""
+    import mlx_batch_invariant_b200 as bi
+    from mlx_batch_invariant_b200 import decoder as dec
+    with bi.batch_invariant_mode(strict=True):
+        eager = _slot0(model, 3)
+        graph = dec.DecodeGraph(model, 3)
+        ids = dec.prompts(model.cfg, 3, 37, "cuda")
+        logits, _, _ = dec.generate(model, ids, 6, graph)
+        assert dec.differing(dec.slot0_bits(logits), eager) == [0] * eager.shape[0]
+        g1 = dec.DecodeGraph(model, 1)
+        logits1, _, _ = dec.generate(model, ids[:1], 6, g1)
+        assert dec.differing(dec.slot0_bits(logits1), eager) == [0] * eager.shape[0]

@@ -248,3 +248,26 @@ def test_decoder_sharding_plan_matches_one_process():
             (q[r * hq:(r + 1) * hq], k[r * hk:(r + 1) * hk], v[r * hk:(r + 1) * hk])))
         half = cfg.hidden // 2
         np.testing.assert_array_equal(got["wd"], single.layers[1]["wd"].numpy()[r * half:(r + 1) * half])
+
+
+def test_decoder_static_step_matches_eager_decode_on_cpu():
+    """The graph-capturable step (device position, index_copy_ cache write, masked
+    full-cache attention, on-device argmax and position advance) follows the eager
+    decode on one process (stock float32 ops on CPU: close, same greedy tokens)."""
+    _setup_paths()
+    from mlx_batch_invariant_b200 import decoder as dec
+    cfg = dec.DecoderConfig(**TINY_DECODER)
+    model = dec.Decoder(cfg, max_batch=2, max_len=12, dtype=torch.float32, device="cpu",
+                        single=True)
+    ids = dec.prompts(cfg, 2, 6, "cpu")
+    eager = _greedy(model, ids, 4)
+    first = model.prefill(ids)
+    tok = first.argmax(dim=-1, keepdim=True)
+    pos = torch.tensor([model.pos])
+    steps = [first]
+    for _ in range(4):
+        steps.append(model._greedy_step(tok, pos))
+    static = torch.stack(steps)
+    assert pos.item() == 10 and model.pos == 6
+    np.testing.assert_allclose(static.numpy(), eager.numpy(), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(static.argmax(-1).numpy(), eager.argmax(-1).numpy())
