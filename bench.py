@@ -509,7 +509,7 @@ def _bench_sdpa(bi, parallel, world, rank, dev, peaks, args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "traffic": traffic if world == 1 else None,
-                         "kernel": "sdpa_kernel<bf16, D=128, LP=8, HG=2, stages=3, rows=2>"},
+                         "kernel": "sdpa_mma_kernel<bf16, D=128, GH=4> (tensor-core route)"},
             "stock_sdpa_gbs": stock_gbs}
 
 

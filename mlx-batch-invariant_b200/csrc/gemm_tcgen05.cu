@@ -586,6 +586,35 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+}  // namespace tc
+
+int encode_tiled16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides, const uint32_t* box, int dtype) {
+  tc::EncodeTiledFn enc = tc::get_encode_fn();
+  if (!enc) return set_error(BI_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const CUtensorMapDataType dt =
+      dtype == BI_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+    if (i > 0) st[i - 1] = strides[i - 1];
+  }
+  CUresult r = enc(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, bx,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return set_error(BI_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d), rank %d",
+                     static_cast<int>(r), rank);
+  }
+  return BI_OK;
+}
+
+namespace tc {
+
 // 2-D tensor map over a row-major (rows, cols) matrix of 16-bit elements with the
 // given row stride (elements), box (box_cols x box_rows), 128-byte swizzle, and
 // zero fill outside the matrix.

@@ -1,6 +1,7 @@
 // Host-side interfaces between the translation units of libbi.so.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -70,6 +71,11 @@ constexpr int kTcBK = 64;
 constexpr int kSimtBM = 128;
 constexpr int kSimtBN = 128;
 constexpr int kSimtBK = 8;
+
+// Tiled TMA descriptor over 16-bit data of `rank` dims (innermost first), strides in
+// bytes for dims 1.., 128-byte swizzle, zero fill outside.  Defined with the GEMM.
+int encode_tiled16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides, const uint32_t* box, int dtype);
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
 // g.out points at column cols[rank] of the output whose first column is out_base.

@@ -6,8 +6,10 @@
 // whole reduction over the N keys.  Key i always folds into partial p = i % 32.
 // Each partial keeps an fp32 online-softmax state (running max m, denominator l,
 // numerator o[V]); the 32 partials are then combined in the fixed order p = 0..31.
-// Nothing depends on B, H, qL or on the other rows in flight: there is no split-KV,
-// no second pass and no route switch, so a token's output has the same bits in
+// Nothing depends on B, qL, N or on the other rows in flight: there is no split-KV,
+// no second pass, and the route (the CUDA-core kernel here, or the tensor-core kernel
+// further down for 16-bit data with D = 64 / 128 and GQA groups of 4k heads) is a
+// function of the model's shapes alone, so a token's output has the same bits in
 // decode and in any chunked prefill, and an extra masked key is a no-op.
 //
 // B200 mapping:
@@ -224,8 +226,7 @@ __global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA
   float* comb_o = reinterpret_cast<float*>(smem);            // [PARTIALS][D], after the walk
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int part = tid / LP;  // meaningful for consumer threads (warp < NW)
+  const int part = tid / LP;
   const int sub = tid % LP;
   const int lane = tid & 31;
   const int part_lane0 = lane & ~(LP - 1);  // first lane of this partial in the warp
@@ -442,6 +443,397 @@ __global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core route: fp16 / bf16, D = 64 or 128.
+//
+// The same fold -- key i belongs to partial i % 32, each partial keeps an fp32
+// online-softmax state, the 32 partials are combined in the fixed order p = 0..31 --
+// with a partial's keys folded a stage at a time.  Keys arrive in stages of 128
+// (4 per partial, at absolute positions fixed by the key index alone), and each
+// (query head h, partial p) takes the visible ones among its 4 at once:
+//     m' = max(m, max_j s_j);  f = exp(m - m');  e_j = exp(s_j - m')
+//     l  = fmaf(l, f, (e_0 + e_1) + (e_2 + e_3));  o = o * f + sum_j e_j v_j
+// (f = 1 exactly when m' == m, and the multiply is skipped; a stage in which none of
+// a partial's keys is visible leaves its state untouched).
+//
+// The products run on the tensor cores with mma.sync m16n8k16 and fp32 accumulation
+// (at decode the pipe is far from busy; the kernel is bound by streaming K and V).
+// MMA rows are (head, partial) pairs, r = pp*GH + h inside a warp of 16 rows, so the
+// GQA group shares every K/V fragment.  A partial's 4 keys of a stage occupy
+// positions 4*j + p % 4 of a 16-key MMA step, for every GQA factor; the other
+// positions of the row carry exact zeros.  s = scale * (q . k) with q and k as
+// given; e enters the second product as e_hi + e_lo, two 16-bit values holding ~16
+// significant bits.  K and V stages come in by 4-D TMA (128-byte swizzle, zero fill
+// past N), one TMA box per 64 columns.
+namespace tcr {
+
+constexpr int R = 4;                 // keys per partial per stage
+constexpr int KEYS = PARTIALS * R;   // keys per stage
+constexpr int BOX_D = 64;            // columns per TMA box (128-byte rows)
+
+template <int D>
+struct Plan {
+  static constexpr int BOXES = D / BOX_D;
+  static constexpr int TSB = KEYS * D * 2;               // one tensor's stage bytes
+  static constexpr int STAGES = D == 128 ? 3 : 4;
+  static constexpr int SMEM = 1024 + 2 * STAGES * TSB + STAGES * 8 + 64;
+  static_assert(SMEM <= 227 * 1024, "shared memory above the per-CTA limit");
+};
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (dtype_of<T>::value == 2) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Shared-memory address of the 16-byte chunk holding columns [d, d + 8) of stage row
+// `row`: one TMA box per 64 columns (KEYS rows of 128 B), chunks swizzled by row % 8.
+__device__ __forceinline__ uint32_t kv_addr(uint32_t base, int row, int d) {
+  const int box = d >> 6;
+  const int c = (d & 63) >> 3;
+  return base + box * (KEYS * 128) + row * 128 + ((c ^ (row & 7)) << 4);
+}
+
+// Two fp32 values -> one register of two 16-bit T (round to nearest even), and what
+// the rounding left over.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_rn(float lo, float hi, float& rlo, float& rhi) {
+  uint32_t r;
+  if constexpr (dtype_of<T>::value == 2) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    rlo = __fsub_rn(lo, __low2float(v));
+    rhi = __fsub_rn(hi, __high2float(v));
+    r = *reinterpret_cast<const uint32_t*>(&v);
+  } else {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    rlo = __fsub_rn(lo, __low2float(v));
+    rhi = __fsub_rn(hi, __high2float(v));
+    r = *reinterpret_cast<const uint32_t*>(&v);
+  }
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
+  float a, b;
+  return pack_rn<T>(lo, hi, a, b);
+}
+
+template <typename T, int D, int GH>
+__global__ void __launch_bounds__(64 * GH, 1)
+    sdpa_mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                    const Params p) {
+  using PL = Plan<D>;
+  constexpr int NW = 2 * GH;         // warps: 16 MMA rows each
+  constexpr int NT = 32 * NW;
+  constexpr int NPW = 16 / GH;       // partials per warp
+  constexpr int KG = NPW / 4;        // 16-key MMA steps per warp per stage
+  constexpr int KSTEPS = D / 16;     // MMA k-steps over the head dim
+  constexpr int NTD = D / 8;         // n-tiles of the output row
+  constexpr int STAGES = PL::STAGES;
+  constexpr int TSB = PL::TSB;
+  static_assert(KSTEPS % 2 == 0 && NTD % 2 == 0, "fragments are loaded in pairs");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + STAGES * TSB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * STAGES * TSB);
+  int* done_count = reinterpret_cast<int*>(full + STAGES);
+  int* issued_count = done_count + STAGES;
+  volatile int* abort_flag = issued_count + 1;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int gq = lane >> 2;  // MMA group: this thread's rows gq and gq + 8
+  const int q4 = lane & 3;
+
+  const int groups = p.H / GH;
+  int idx = blockIdx.x;
+  const int s = idx % p.qL;
+  idx /= p.qL;
+  const int hg = idx % groups;
+  const int b = idx / groups;
+  const int h0 = hg * GH;
+  const int kvh = h0 / (p.H / p.Hkv);
+
+  int64_t kmax = p.N;
+  if (p.mask_mode == 1) {
+    const int64_t last = p.causal_offset + s;
+    kmax = last < 0 ? 0 : (last + 1 < p.N ? last + 1 : p.N);
+  }
+  const int nblocks = static_cast<int>((kmax + KEYS - 1) / KEYS);
+
+  // This thread's two rows: same head, partials part[0] and part[1].
+  const int head = gq % GH;
+  int pp[2] = {gq / GH, (gq + 8) / GH};
+  int part[2] = {warp * NPW + pp[0], warp * NPW + pp[1]};
+
+  const T* Q = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.qs0 +
+               static_cast<int64_t>(h0 + head) * p.qs1 + static_cast<int64_t>(s) * p.qs2;
+  uint32_t qa[KSTEPS][2];
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk) {
+    qa[kk][0] = *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 2 * q4);
+    qa[kk][1] = *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 8 + 2 * q4);
+  }
+  const T* Mk = static_cast<const T*>(p.mask);
+  const T* mrow = Mk == nullptr ? nullptr
+                                : Mk + static_cast<int64_t>(b) * p.ms0 +
+                                      static_cast<int64_t>(h0 + head) * p.ms1 +
+                                      static_cast<int64_t>(s) * p.ms2;
+
+  float o[NTD][4];
+#pragma unroll
+  for (int nd = 0; nd < NTD; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m[2] = {-3.40282347e+38f, -3.40282347e+38f};
+  float l[2] = {0.f, 0.f};
+  const T* Sk = static_cast<const T*>(p.sinks);
+  if (Sk != nullptr) {
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      if (part[ri] == 0) {
+        m[ri] = to_f32(Sk[h0 + head]);
+        l[ri] = 1.f;
+      }
+    }
+  }
+
+  auto issue = [&](int blk) {
+    const int st = blk % STAGES;
+    mbar_arrive_expect_tx(&full[st], 2 * TSB);
+#pragma unroll
+    for (int bx = 0; bx < PL::BOXES; ++bx) {
+      tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh,
+                  b);
+      tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh,
+                  b);
+    }
+  };
+
+  if (tid == 0) {
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      done_count[st] = 0;
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    int n0 = 0;
+    for (; n0 < STAGES && n0 < nblocks; ++n0) issue(n0);
+    *issued_count = n0;
+  }
+  __syncthreads();
+
+  const float scale = p.scale;
+  bool aborted = false;
+  for (int t = 0; t < nblocks; ++t) {
+    const int st = t % STAGES;
+    bool ok = mbar_wait(&full[st], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
+      }
+      aborted = true;
+      break;
+    }
+    const uint32_t kbase = smem_u32(sK + st * TSB);
+    const uint32_t vbase = smem_u32(sV + st * TSB);
+    const int64_t key0 = static_cast<int64_t>(t) * KEYS;
+#pragma unroll
+    for (int g = 0; g < KG; ++g) {
+      const int pbase = warp * NPW + 4 * g;  // first partial of this MMA step
+      // ---- scores: 16 rows x 16 key positions (position = 4 * j + partial % 4)
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const int pos = 8 * nt + (lane & 7);
+        const int krow = 32 * (pos >> 2) + pbase + (pos & 3);
+        const int mi = lane >> 3;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; kk += 2) {
+          uint32_t bf[4];
+          ldsm_x4(bf, kv_addr(kbase, krow, 16 * (kk + (mi >> 1)) + 8 * (mi & 1)));
+          mma16816<T>(sc[nt], qa[kk][0], qa[kk][0], qa[kk][1], qa[kk][1], bf[0], bf[1]);
+          mma16816<T>(sc[nt], qa[kk + 1][0], qa[kk + 1][0], qa[kk + 1][1], qa[kk + 1][1], bf[2],
+                      bf[3]);
+        }
+      }
+      // ---- stage update of each of this thread's rows whose partial is in this step.
+      // Element (nt, e) of row ri is position 8*nt + 2*q4 + e; it is one of the row's
+      // keys when that position % 4 == the row's partial % 4, i.e. when
+      // (q4 & 1) == want >> 1 and e == want & 1; its j is 2*nt + (q4 >> 1).
+      uint32_t phi[4], plo[4];
+#pragma unroll
+      for (int ri = 0; ri < 2; ++ri) {
+        const bool mine = (pp[ri] >> 2) == g;
+        const int want = pp[ri] & 3;
+        const bool holder = mine && (q4 & 1) == (want >> 1);
+        float x[2];
+        bool use[2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int j = 2 * nt + (q4 >> 1);
+          const int64_t key = key0 + 32 * j + pbase + want;
+          bool u = holder && key < kmax;
+          float v = __fmul_rn(sc[nt][2 * ri + (want & 1)], scale);
+          if (u && p.mask_mode == 2) {
+            const float bias = to_f32(mrow[key]);
+            u = bias > -3.0e38f;
+            v = __fadd_rn(v, bias);
+          }
+          use[nt] = u;
+          x[nt] = v;
+        }
+        float mx = use[0] ? x[0] : -INFINITY;
+        if (use[1]) mx = fmaxf(mx, x[1]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        // Whether some key of the row is visible is uniform over the quad, not over the
+        // warp, so every shuffle below runs unconditionally and only the state update
+        // is guarded.
+        const bool any = mx != -INFINITY;
+        const float mn = any ? fmaxf(m[ri], mx) : m[ri];
+        float e[2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) e[nt] = use[nt] ? expf(__fsub_rn(x[nt], mn)) : 0.f;
+        // (e_0 + e_1) + (e_2 + e_3): j = 2*nt + (q4 >> 1); lanes q4 and q4 ^ 2 hold
+        // j and j ^ 1 of the same nt.
+        const float u0 = __fadd_rn(e[0], __shfl_xor_sync(0xffffffffu, e[0], 2));
+        const float u1 = __fadd_rn(e[1], __shfl_xor_sync(0xffffffffu, e[1], 2));
+        const float sum =
+            __shfl_sync(0xffffffffu, __fadd_rn(u0, u1), (lane & ~3) | (want >> 1));
+        if (any) {
+          const float f = mn == m[ri] ? 1.0f : expf(__fsub_rn(m[ri], mn));
+          l[ri] = __fmaf_rn(l[ri], f, sum);
+          if (f != 1.0f) {
+#pragma unroll
+            for (int nd = 0; nd < NTD; ++nd) {
+              o[nd][2 * ri] = __fmul_rn(o[nd][2 * ri], f);
+              o[nd][2 * ri + 1] = __fmul_rn(o[nd][2 * ri + 1], f);
+            }
+          }
+          m[ri] = mn;
+        }
+        // this row's weights at its positions (nt, e = want & 1), zero elsewhere
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float w0 = (want & 1) == 0 ? e[nt] : 0.f;
+          const float w1 = (want & 1) == 1 ? e[nt] : 0.f;
+          float r0, r1;
+          phi[2 * nt + ri] = pack_rn<T>(w0, w1, r0, r1);
+          plo[2 * nt + ri] = pack_rn<T>(r0, r1);
+        }
+      }
+      // ---- o += P V over this step's 16 keys (P = P_hi + P_lo)
+      const int mi = lane >> 3;
+      const int vpos = 8 * (mi & 1) + (lane & 7);
+      const int vrow = 32 * (vpos >> 2) + pbase + (vpos & 3);
+#pragma unroll
+      for (int nd = 0; nd < NTD; nd += 2) {
+        uint32_t bv[4];
+        ldsm_x4_t(bv, kv_addr(vbase, vrow, 8 * (nd + (mi >> 1))));
+        mma16816<T>(o[nd], phi[0], phi[1], phi[2], phi[3], bv[0], bv[1]);
+        mma16816<T>(o[nd], plo[0], plo[1], plo[2], plo[3], bv[0], bv[1]);
+        mma16816<T>(o[nd + 1], phi[0], phi[1], phi[2], phi[3], bv[2], bv[3]);
+        mma16816<T>(o[nd + 1], plo[0], plo[1], plo[2], plo[3], bv[2], bv[3]);
+      }
+    }
+    // The last warp done with this stage refills it with block t + STAGES.
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&done_count[st], 1) == NW - 1) {
+        __threadfence_block();
+        done_count[st] = 0;
+        if (t + STAGES < nblocks && !*abort_flag) {
+          fence_proxy_async_smem();
+          issue(t + STAGES);
+          atomicMax(issued_count, t + STAGES + 1);
+        }
+      }
+    }
+  }
+  if (__syncthreads_or(aborted)) {
+    if (tid == 0) {
+      const int issued = *issued_count;
+      for (int blk = issued - STAGES < 0 ? 0 : issued - STAGES; blk < issued; ++blk) {
+        mbar_wait(&full[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
+      }
+    }
+    return;
+  }
+  __syncthreads();  // every stage consumed and no copy in flight: the ring is free
+
+  // ---- combine the 32 partials of every head, p = 0..31
+  float* comb_o = reinterpret_cast<float*>(smem);               // [GH][32][D]
+  float* comb_m = comb_o + GH * PARTIALS * D;                   // [GH][32]
+  float* comb_l = comb_m + GH * PARTIALS;                       // [GH][32]
+#pragma unroll
+  for (int ri = 0; ri < 2; ++ri) {
+    float* row = comb_o + (head * PARTIALS + part[ri]) * D;
+#pragma unroll
+    for (int nd = 0; nd < NTD; ++nd) {
+      *reinterpret_cast<float2*>(row + 8 * nd + 2 * q4) = make_float2(o[nd][2 * ri], o[nd][2 * ri + 1]);
+    }
+    if (q4 == 0) {
+      comb_m[head * PARTIALS + part[ri]] = m[ri];
+      comb_l[head * PARTIALS + part[ri]] = l[ri];
+    }
+  }
+  __syncthreads();
+  T* O = static_cast<T*>(p.out);
+  for (int jj = tid; jj < GH * D; jj += NT) {
+    const int hh = jj / D;
+    const int j = jj - hh * D;
+    const float* cm = comb_m + hh * PARTIALS;
+    const float* cl = comb_l + hh * PARTIALS;
+    float mx = cm[0];
+#pragma unroll
+    for (int q = 1; q < PARTIALS; ++q) mx = fmaxf(mx, cm[q]);
+    float lsum = 0.f, acc = 0.f;
+#pragma unroll 4
+    for (int q = 0; q < PARTIALS; ++q) {
+      const float fq = expf(__fsub_rn(cm[q], mx));
+      lsum = __fmaf_rn(cl[q], fq, lsum);
+      acc = __fmaf_rn(comb_o[(hh * PARTIALS + q) * D + j], fq, acc);
+    }
+    const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
+    O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + hh) * p.os1 +
+      static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
+  }
+}
+
+}  // namespace tcr
+
 // Threads per partial: 32 bytes of a key row per thread where the row allows, a power
 // of two that divides D, at most 16 (CTAs of at most 512 threads).  A function of
 // (D, dtype) only.
@@ -532,8 +924,70 @@ static int launch_d(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   return launch_hg<T, D, 1>(p, blocks, stream);
 }
 
+namespace tcr {
+
+// K or V as a 4-D TMA map (D, N, Hkv, B): rows of a head are contiguous; a dimension
+// of extent 1 gets a compact stride, any other must be a positive multiple of 16 B.
+template <int D>
+static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], const SdpaArgs& a) {
+  const uint64_t rows = a.N > 0 ? static_cast<uint64_t>(a.N) : 1;
+  uint64_t dims[4] = {static_cast<uint64_t>(D), rows, static_cast<uint64_t>(a.Hkv),
+                      static_cast<uint64_t>(a.B)};
+  uint64_t strides[3] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(st[1]) * 2,
+                         static_cast<uint64_t>(st[0]) * 2};
+  if (dims[2] == 1) strides[1] = strides[0] * dims[1];
+  if (dims[3] == 1) strides[2] = strides[1] * dims[2];
+  for (int i = 1; i < 3; ++i) {
+    if (strides[i] == 0 || strides[i] % 16 != 0) {
+      return set_error(BI_ERR_MISALIGNED, "k/v head and batch strides must be positive "
+                                          "multiples of 8 elements");
+    }
+  }
+  uint32_t box[4] = {BOX_D, KEYS, 1, 1};
+  return encode_tiled16(map, base, 4, dims, strides, box, a.dtype);
+}
+
+template <typename T, int D, int GH>
+static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  using PL = Plan<D>;
+  CUtensorMap tk, tv;
+  int st = kv_map<D>(&tk, a.k, a.ks, a);
+  if (st) return st;
+  st = kv_map<D>(&tv, a.v, a.vs, a);
+  if (st) return st;
+  auto kern = sdpa_mma_kernel<T, D, GH>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PL::SMEM);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa tc)");
+  const int64_t blocks = a.B * (a.H / GH) * a.qL;
+  if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "too many attention rows");
+  kern<<<static_cast<unsigned>(blocks), 64 * GH, PL::SMEM, stream>>>(tk, tv, p);
+  return cuda_status(cudaGetLastError(), "sdpa tc launch");
+}
+
+// Four query heads per CTA (a GQA group of 4k heads takes k CTAs); the kernel is
+// written for any of 1, 2 or 4 heads per CTA, which only decides which CTA computes
+// a row, but only 4 is routed here.
+template <typename T, int D>
+static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  return launch_gh<T, D, 4>(a, p, stream);
+}
+
+}  // namespace tcr
+
+// Route: fp16 / bf16 with D = 64 or 128 and every KV head shared by a multiple of 4
+// query heads take the tensor-core kernel (its MMA rows are the 4 heads x partials, so
+// each K/V fragment serves 4 rows); everything else the CUDA-core one.  The route is a
+// function of the model's shapes (dtype, D, H / Hkv) only -- never of B, qL or N -- so
+// a token's bits are the same in decode and in any chunked prefill.
 template <typename T>
 static int launch_t(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    if ((a.H / a.Hkv) % 4 == 0) {
+      if (a.D == 64) return tcr::launch<T, 64>(a, p, stream);
+      if (a.D == 128) return tcr::launch<T, 128>(a, p, stream);
+    }
+  }
   switch (a.D) {
     case 32: return launch_d<T, 32>(a, p, stream);
     case 64: return launch_d<T, 64>(a, p, stream);

@@ -59,7 +59,10 @@ def _aligned_heads(t, row_contiguous):
     es = t.element_size()
     vec = 16 // es
     ok = t.stride(-1) == 1 and t.data_ptr() % 16 == 0
-    ok = ok and all(s % vec == 0 for s in t.stride()[:-1])
+    # (a zero stride over an extent above 1 -- an expanded tensor -- is copied too:
+    # the tensor-core route reads k and v through TMA, which needs real strides)
+    ok = ok and all(s % vec == 0 and (s > 0 or n == 1)
+                    for s, n in zip(t.stride()[:-1], t.shape[:-1]))
     if row_contiguous:
         ok = ok and (t.shape[2] <= 1 or t.stride(2) == t.shape[3])
     if not ok:

@@ -1,8 +1,11 @@
 """GPU parity and invariance tests of the batch-invariant attention (libbi.so bi_sdpa).
 
-Parity bar against the host oracle (same fold, same lane split, C-library expf in
-place of CUDA's expf): max |gpu - oracle| / max |oracle| <= 2e-6 for float32 and
-<= 1 ulp of the output type (relative to the row scale) for float16 / bfloat16.
+Parity bar against the host oracle (the reference's per-key fold; the CUDA-core route
+runs that fold with the oracle's lane split, the tensor-core route -- 16-bit, D = 64 /
+128, GQA groups of 4k heads -- folds each partial's keys a stage of 4 at a time with
+tensor-core products; C-library expf in place of CUDA's): max |gpu - oracle| /
+max |oracle| <= 2e-6 for float32 and <= 1 ulp of the output type (relative to that
+scale) for float16 / bfloat16.
 Accuracy against float64 follows the reference (tests/test_invariance.py:408-432):
 float32 < 2e-6, bfloat16 < 3e-2.  Invariance bar: 0 differing bits.
 """
