@@ -27,6 +27,7 @@ Also reported:
 --impl reference times that CPU implementation alone on the same metric (rank 0).
 --profile gemm|sdpa runs 3 warm-up launches and 1 launch of one kernel at the bench's
 own dominant shape and prints nothing (the target of the committed ncu captures).
+--sweep prints config 5's table: bi.linear vs cuBLAS at M in 1..16384 on every shape.
 """
 
 import argparse
@@ -538,6 +539,54 @@ def run_profile(args):
     return 0
 
 
+SWEEP_M = (1, 8, 64, 512, 4096, 16384)
+
+
+def run_sweep(args):
+    """Config 5's sweep on one GPU: bi.linear and stock F.linear (cuBLAS) at every
+    (K, N) of SHAPES and M in SWEEP_M, bf16; one markdown table on stdout.  Every
+    weight exceeds L2 (>= 134 MB), so a GEMM re-reads it from HBM each launch."""
+    import mlx_batch_invariant_b200 as bi
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    peaks, src = _peaks()
+    peak, hbm = peaks["bf16_tflops"], peaks["hbm_gbs"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / 1e3
+
+    print("| K | N | M | bi.linear µs | TFLOP/s | of tensor peak | HBM GB/s | cuBLAS µs | bi / cuBLAS |")
+    print("|---|---|---|---|---|---|---|---|---|")
+    for K, N in SHAPES:
+        w = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        for Mr in SWEEP_M:
+            x = torch.randn((Mr, K), generator=g, device=dev).to(torch.bfloat16)
+            reps = 20 if Mr < 4096 else 5
+            t_bi = timed(lambda: bi.linear(x, w), reps)
+            t_cb = timed(lambda: torch.nn.functional.linear(x, w), reps)
+            flops = 2.0 * Mr * N * K
+            moved = 2.0 * (Mr * K + N * K + Mr * N)
+            print("| %d | %d | %d | %.1f | %.1f | %.1f %% | %.0f | %.1f | %.2f |"
+                  % (K, N, Mr, t_bi * 1e6, flops / t_bi / 1e12, 100 * flops / t_bi / 1e12 / peak,
+                     moved / t_bi / 1e9, t_cb * 1e6, t_cb / t_bi), flush=True)
+            del x
+        del w
+    print("\npeaks: %s (bf16 %.0f TFLOP/s burst, HBM %.0f GB/s); bi / cuBLAS > 1 means "
+          "bi.linear is faster" % (src, peak, hbm))
+    return 0
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description="batch-invariant kernel throughput")
     p.add_argument("--gpus", type=int, default=1)
@@ -546,9 +595,13 @@ def main(argv=None):
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile", choices=["gemm", "sdpa"], default=None)
+    p.add_argument("--sweep", action="store_true",
+                   help="config 5's M sweep on one GPU (a markdown table, no JSON line)")
     args = p.parse_args(argv)
     if args.profile:
         return run_profile(args)
+    if args.sweep:
+        return run_sweep(args)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":
