@@ -7,8 +7,11 @@
 // k ascending; each slice is summed in order into a fresh fp32 partial with fmaf
 // (p = fmaf(a[k], b[k], p)), and the partial is added to the fp32 accumulator
 // (acc = acc + p).  This is exactly the host oracle's order, so the route is bit-exact
-// against it.  The 128 x 128 x 8 CTA tile is fixed, each CTA owns the whole K
-// reduction, and nothing in the arithmetic depends on M.
+// against it.  Each output element is one thread's sequence of scalar operations, so
+// the thread layout cannot change a bit: a 128 x 128 x 8 CTA tile in general, and for
+// up to 64 rows with (N, K) weights a warp per output column (gemm_simt_rows_kernel).
+// Each element's K reduction stays in one thread; nothing in the arithmetic depends
+// on M.
 #include "common.cuh"
 #include "internal.h"
 
@@ -163,6 +166,112 @@ __global__ void __launch_bounds__(NUM_THREADS) gemm_simt_kernel(const Params p) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Few rows (M <= ROWS_MAX_M = 64), (N, K) weights: one warp per output column.
+//
+// Same arithmetic per element as gemm_simt_kernel -- slice partials p_s =
+// fmaf-chain over k = 8s..8s+7 (zero past K) from a fresh +0, then acc = acc + p_s in
+// slice order -- laid out for streaming W: lane l computes the partials of slices
+// 32c + l of every row from one coalesced 32-byte read of the column's weight row, the
+// partials go through shared memory, and lane m adds row m's in order.  The tiled
+// kernel above pads M to 128 rows per CTA; this one reads each weight once per column.
+constexpr int ROWS_MAX_M = 64;
+// Warps per CTA for a MAXM-row instantiation: the partials buffer stays 33 KB.
+constexpr int rows_warps(int maxm) { return 256 / maxm; }
+
+// Elements k0 .. k0+7 of a row as fp32, zero past K.  VEC: the 8 elements are one
+// aligned 16- or 32-byte run whenever k0 + 8 <= K.
+template <typename T, bool VEC>
+__device__ __forceinline__ void load8(const T* row, int k0, int K, float (&v)[8]) {
+  if (VEC && k0 + 8 <= K) {
+    if constexpr (sizeof(T) == 4) {
+      const float4 x = *reinterpret_cast<const float4*>(row + k0);
+      const float4 y = *reinterpret_cast<const float4*>(row + k0 + 4);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+      v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+    } else {
+      const uint4 x = *reinterpret_cast<const uint4*>(row + k0);
+      const T* h = reinterpret_cast<const T*>(&x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = to_f32(h[j]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = (k0 + j < K) ? to_f32(row[k0 + j]) : 0.f;
+}
+
+// Chunks of 32 slices whose weights a lane keeps in flight ahead of the one it uses.
+constexpr int ROWS_PREFETCH = 4;
+
+// MAXM (32 or 64): the rows this instantiation holds; lane l folds rows l and l + 32.
+template <typename T, bool VEC, int MAXM>
+__global__ void __launch_bounds__(32 * rows_warps(MAXM)) gemm_simt_rows_kernel(const Params p) {
+  constexpr int RB = MAXM / 32;  // rows folded per lane
+  constexpr int ROWS_WARPS = rows_warps(MAXM);
+  __shared__ float part_s[ROWS_WARPS][MAXM][33];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = blockIdx.x * ROWS_WARPS + warp;
+  if (n >= p.N) return;  // whole warps only; no CTA-wide barrier follows
+  const T* A = static_cast<const T*>(p.a);
+  const T* Bn = static_cast<const T*>(p.b) + static_cast<int64_t>(n) * p.ldb;
+  const int slices = (p.K + BK - 1) / BK;
+  float (*ps)[33] = part_s[warp];
+  float acc[RB];  // acc[r]: row lane + 32 r
+#pragma unroll
+  for (int r = 0; r < RB; ++r) acc[r] = 0.f;
+  float w[ROWS_PREFETCH][8];  // slot u holds the weights of chunk (index mod PF) == u
+#pragma unroll
+  for (int u = 0; u < ROWS_PREFETCH; ++u) load8<T, VEC>(Bn, BK * (32 * u + lane), p.K, w[u]);
+  for (int c0 = 0; c0 < slices; c0 += 32 * ROWS_PREFETCH) {
+#pragma unroll
+    for (int u = 0; u < ROWS_PREFETCH; ++u) {
+      const int cc = c0 + 32 * u;  // first slice of this chunk (warp-uniform)
+      if (cc < slices) {
+        const int s = cc + lane;
+        for (int m = 0; m < p.M; ++m) {
+          float a[8];
+          load8<T, VEC>(A + static_cast<int64_t>(m) * p.lda, BK * s, p.K, a);
+          float part = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) part = __fmaf_rn(a[j], w[u][j], part);
+          ps[m][lane] = part;
+        }
+        // refill the slot with the chunk PF ahead (zeros past K)
+        load8<T, VEC>(Bn, BK * (s + 32 * ROWS_PREFETCH), p.K, w[u]);
+        __syncwarp();
+        const int cnt = slices - cc < 32 ? slices - cc : 32;
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          const int row = lane + 32 * r;
+          if (row < p.M) {
+            // all 32 loads first, then the adds strictly in slice order
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = ps[row][i];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i < cnt) acc[r] = __fadd_rn(acc[r], v[i]);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  const T* bias = static_cast<const T*>(p.bias);
+  const float bj = p.has_bias ? to_f32(bias[n]) : 0.f;
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const int row = lane + 32 * r;
+    if (row < p.M) {
+      static_cast<T*>(p.out)[static_cast<int64_t>(row) * p.ldo + n] =
+          gemm_epilogue<T>(acc[r], p.has_bias, p.alpha, p.beta, bj);
+    }
+  }
+}
+
 template <typename T, bool B_NK>
 static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   Params p;
@@ -179,6 +288,27 @@ static int launch_typed(const GemmArgs& g, cudaStream_t stream) {
   p.alpha = g.alpha;
   p.beta = g.beta;
   p.has_bias = g.bias != nullptr;
+  if (B_NK && g.M <= ROWS_MAX_M) {
+    // few rows: one warp per column (same per-element arithmetic as the tiled kernel)
+    const int maxm = g.M <= 32 ? 32 : 64;
+    const int64_t blocks = (g.N + rows_warps(maxm) - 1) / rows_warps(maxm);
+    if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "N too large");
+    const size_t es = sizeof(T);
+    const bool vec = (reinterpret_cast<uintptr_t>(g.a) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(g.b) % 16 == 0) && (g.lda * es) % 16 == 0 &&
+                     (g.ldb * es) % 16 == 0;
+    const unsigned nb = static_cast<unsigned>(blocks);
+    if (maxm == 32) {
+      constexpr int nt = 32 * rows_warps(32);
+      if (vec) gemm_simt_rows_kernel<T, true, 32><<<nb, nt, 0, stream>>>(p);
+      else gemm_simt_rows_kernel<T, false, 32><<<nb, nt, 0, stream>>>(p);
+    } else {
+      constexpr int nt = 32 * rows_warps(64);
+      if (vec) gemm_simt_rows_kernel<T, true, 64><<<nb, nt, 0, stream>>>(p);
+      else gemm_simt_rows_kernel<T, false, 64><<<nb, nt, 0, stream>>>(p);
+    }
+    return cuda_status(cudaGetLastError(), "gemm_simt rows launch");
+  }
   const int64_t gy = (g.M + BM - 1) / BM;
   const int64_t gx = (g.N + BN - 1) / BN;
   if (gy > 65535) return set_error(BI_ERR_UNSUPPORTED, "M too large for the CUDA-core route");
