@@ -392,24 +392,60 @@ def run_ours(args):
     h2d = sum(t.numel() * t.element_size() for t in hx.values())
     d2h = sum(t.numel() * t.element_size() for t in hy)
 
-    def e2e_step():
-        dx = {K: hx[K].to(dev, non_blocking=True) for K in hx}
+    # Copies run on their own streams (the copy engines; PCIe is full duplex) and overlap
+    # the GEMMs: step it copies its inputs into device buffer it % 2 while the GEMMs
+    # of step it - 1 run, and each output starts back to the host as soon as its GEMM
+    # is done.  Every byte is still copied every step inside the timed region.
+    copy_in, copy_out = torch.cuda.Stream(), torch.cuda.Stream()
+    dx_bufs = [{K: torch.empty_like(xs[K]) for K in xs} for _ in range(2)]
+    dy_bufs = [[torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _, N in SHAPES]
+               for _ in range(2)] if world > 1 else None
+    freed = [torch.cuda.Event() for _ in range(2)]  # last GEMM reading dx_bufs[b] done
+    drained = [[torch.cuda.Event() for _ in SHAPES] for _ in range(2)]  # D2H of output b, i
+    for b in range(2):
+        freed[b].record(main)
+        for e in drained[b]:
+            e.record(main)
+
+    def e2e_step(it):
+        b = it & 1
+        dx = dx_bufs[b]
+        ready = {}
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(freed[b])
+            for K in hx:
+                dx[K].copy_(hx[K], non_blocking=True)
+                ready[K] = torch.cuda.Event()
+                ready[K].record(copy_in)
         for i, (K, N) in enumerate(SHAPES):
+            main.wait_event(ready[K])
             if world > 1:
-                y = fused[i].linear(dx[K], ws[i], out=ys[i])
+                main.wait_event(drained[b][i])
+                y = fused[i].linear(dx[K], ws[i], out=dy_bufs[b][i])
             else:
                 y = bi.linear(dx[K], ws[i])
-            hy[i].copy_(y, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(main)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done)
+                hy[i].copy_(y, non_blocking=True)
+                y.record_stream(copy_out)
+                drained[b][i].record(copy_out)
+        freed[b].record(main)
 
     e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
+    for it in range(2):
+        e2e_step(it)
+    main.wait_stream(copy_out)
     _barrier_sync(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    f1.record()
+    f0.record(main)
+    copy_in.wait_stream(main)
+    for it in range(e2e_steps):
+        e2e_step(it)
+    main.wait_stream(copy_out)
+    main.wait_stream(copy_in)
+    f1.record(main)
     _barrier_sync(world)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
     e2e_value = FLOPS_PER_STEP * e2e_steps / (e2e_ms / 1e3) / 1e12
@@ -432,6 +468,8 @@ def run_ours(args):
                    else "single GPU",
                    "l2": "inputs larger than L2 (1.7 GB of weights), no flush"},
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "copies": "pinned host buffers; H2D and D2H on their own streams, "
+                          "overlapping the GEMMs (device inputs double-buffered)",
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
