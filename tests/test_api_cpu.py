@@ -203,3 +203,31 @@ def test_nesting_restores_only_at_the_outermost_exit():
         assert torch.matmul is patched, "inner exit unpatched too early"
         assert bi.is_enabled()
     assert torch.matmul is stock
+
+
+def _gather_call(L, cols, world=2, rank=0, stages_null=False, ldo=None, dtype=None):
+    vp = ctypes.c_void_p
+    n_total = cols[-1]
+    stages = None if stages_null else (vp * world)(*([16] * world))
+    flags = (vp * world)(*([256] * world))
+    c = (ctypes.c_int64 * len(cols))(*cols)
+    return L.bi_gemm_allgather(16, 8, 16, 8, None, 16, n_total if ldo is None else ldo,
+                               stages, c, 4, 8, 1, 1.0, 1.0,
+                               _lib.BI_BF16 if dtype is None else dtype, flags, rank, world,
+                               0, None)
+
+
+def test_fused_allgather_validates_its_partition_before_touching_a_device():
+    """bi_gemm_allgather checks the column partition, staging areas and rank set on the
+    host and returns a status (no device needed to reach these errors)."""
+    L = _lib.lib()
+    assert _gather_call(L, [0, 16, 32]) in (0, -6)  # valid; BI_ERR_NO_DEVICE here
+    assert _gather_call(L, [8, 16, 32]) == -1                 # cols[0] != 0
+    assert _gather_call(L, [0, 24, 16]) == -1                 # decreasing
+    assert _gather_call(L, [0, 12, 32]) == -3                 # not a multiple of 8
+    assert b"multiples of 8" in L.bi_last_error()
+    assert _gather_call(L, [0, 16, 32], stages_null=True) == -1
+    assert _gather_call(L, [0, 16, 32], rank=2) == -1          # rank outside the world
+    assert _gather_call(L, [0] * 10, world=9) == -1            # above BI_MAX_PEERS
+    assert _gather_call(L, [0, 16, 32], ldo=24) == -3          # ldo < cols[world]
+    assert _gather_call(L, [0, 16, 32], dtype=_lib.BI_F32) == -2  # tensor-core dtypes only
