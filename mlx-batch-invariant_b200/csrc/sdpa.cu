@@ -196,6 +196,27 @@ __device__ __forceinline__ float reduce_heads(float (&v)[HG], int sub) {
   return v[0];
 }
 
+// Combine weights of one head, computed once by one warp (lane q = partial q): the
+// largest running max M over the 32 partials, f_q = exp(m_q - M) (written over m_q),
+// and the denominator sum_q fmaf(l_q, f_q, .) in the order q = 0..31.  The output
+// loop then only runs its own ordered fmaf chain over the stored f_q.
+__device__ __forceinline__ float combine_weights(float* cm, const float* cl, int lane) {
+  const float mq = cm[lane];
+  float mx = mq;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float fq = expf(__fsub_rn(mq, mx));
+  __syncwarp();
+  cm[lane] = fq;
+  __syncwarp();
+  float lsum = 0.f;
+  if (lane == 0) {
+#pragma unroll 8
+    for (int q = 0; q < PARTIALS; ++q) lsum = __fmaf_rn(cl[q], cm[q], lsum);
+  }
+  return __shfl_sync(0xffffffffu, lsum, 0);
+}
+
 #ifndef BI_SDPA_MIN_BLOCKS
 #define BI_SDPA_MIN_BLOCKS 1
 #endif
@@ -222,7 +243,7 @@ __global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA
   int* issued_count = done_count + STAGES;
   volatile int* abort_flag = issued_count + 1;
   float* comb_m = reinterpret_cast<float*>(done_count + STAGES + 4);  // [PARTIALS]
-  float* comb_l = comb_m + PARTIALS;                         // [PARTIALS]
+  float* comb_l = comb_m + PARTIALS;                         // [PARTIALS + 1]
   float* comb_o = reinterpret_cast<float*>(smem);            // [PARTIALS][D], after the walk
 
   const int tid = threadIdx.x;
@@ -425,17 +446,16 @@ __global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA
       comb_l[part] = l;
     }
     __syncthreads();
+    if (tid < 32) {
+      const float ls = combine_weights(comb_m, comb_l, tid);  // comb_m now holds f_q
+      if (tid == 0) comb_l[PARTIALS] = ls;
+    }
+    __syncthreads();
+    const float lsum = comb_l[PARTIALS];
     for (int j = tid; j < D; j += NT) {
-      float mx = comb_m[0];
-#pragma unroll
-      for (int q = 1; q < PARTIALS; ++q) mx = fmaxf(mx, comb_m[q]);
-      float lsum = 0.f, acc = 0.f;
-#pragma unroll 4
-      for (int q = 0; q < PARTIALS; ++q) {
-        const float fq = expf(__fsub_rn(comb_m[q], mx));
-        lsum = __fmaf_rn(comb_l[q], fq, lsum);
-        acc = __fmaf_rn(comb_o[q * D + j], fq, acc);
-      }
+      float acc = 0.f;
+#pragma unroll 8
+      for (int q = 0; q < PARTIALS; ++q) acc = __fmaf_rn(comb_o[q * D + j], comb_m[q], acc);
       const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
       O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + h) * p.os1 +
         static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
@@ -809,23 +829,22 @@ __global__ void __launch_bounds__(64 * GH, 1)
       comb_l[head * PARTIALS + part[ri]] = l[ri];
     }
   }
+  float* comb_s = comb_l + GH * PARTIALS;                       // [GH] denominators
+  __syncthreads();
+  if (warp < GH) {
+    const float ls = combine_weights(comb_m + warp * PARTIALS, comb_l + warp * PARTIALS, lane);
+    if (lane == 0) comb_s[warp] = ls;  // comb_m now holds the f_q of each head
+  }
   __syncthreads();
   T* O = static_cast<T*>(p.out);
   for (int jj = tid; jj < GH * D; jj += NT) {
     const int hh = jj / D;
     const int j = jj - hh * D;
-    const float* cm = comb_m + hh * PARTIALS;
-    const float* cl = comb_l + hh * PARTIALS;
-    float mx = cm[0];
-#pragma unroll
-    for (int q = 1; q < PARTIALS; ++q) mx = fmaxf(mx, cm[q]);
-    float lsum = 0.f, acc = 0.f;
-#pragma unroll 4
-    for (int q = 0; q < PARTIALS; ++q) {
-      const float fq = expf(__fsub_rn(cm[q], mx));
-      lsum = __fmaf_rn(cl[q], fq, lsum);
-      acc = __fmaf_rn(comb_o[(hh * PARTIALS + q) * D + j], fq, acc);
-    }
+    const float* fq = comb_m + hh * PARTIALS;
+    const float lsum = comb_s[hh];
+    float acc = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < PARTIALS; ++q) acc = __fmaf_rn(comb_o[(hh * PARTIALS + q) * D + j], fq[q], acc);
     const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
     O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + hh) * p.os1 +
       static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
@@ -880,7 +899,7 @@ static int launch_hg(const Params& p, int64_t blocks, cudaStream_t stream) {
   constexpr int R = rows_for<T, D>();
   constexpr int NT = PARTIALS * LP;
   constexpr int smem = 2 * S * PARTIALS * R * D * static_cast<int>(sizeof(T)) + S * 8 +
-                       4 * (S + 4) + 2 * PARTIALS * 4;
+                       4 * (S + 4) + (2 * PARTIALS + 1) * 4;
   static_assert(PARTIALS * D * 4 <= 2 * S * PARTIALS * R * D * static_cast<int>(sizeof(T)),
                 "combine buffer must fit in the stage ring");
   static_assert(smem <= 227 * 1024, "shared memory above the per-CTA limit");
