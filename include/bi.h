@@ -222,6 +222,35 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
                              float alpha, float beta, int dtype, const int* devices,
                              int rank, int world, uint32_t epoch, void* stream);
 
+/*
+ * ---------------------------------------------------------------------------
+ * Elementwise steps of the decoder harness, fused.  No reference counterpart: the
+ * reference's harness (bench/bench.py:108-159) runs its framework's own ops.  Each
+ * output element is computed from its own inputs with the fp32 operations of the
+ * expression named, each rounded, so both are batch-invariant.
+ * ---------------------------------------------------------------------------
+ */
+
+/* Rotary embedding (rotate-half) of the q and k heads of a fused q/k/v projection,
+ * with the KV-cache write:
+ *   qkv    (B, L, (hq + 2 hk) * hd) contiguous: hq query heads, then hk key heads, then
+ *          hk value heads, each hd wide.
+ *   row l of batch b sits at position p = (pos ? *pos : p0) + l (pos: device pointer,
+ *          so a captured graph can advance it);
+ *   q_out  (B, hq, L, hd) contiguous <- rotated q;
+ *   k_cache[b, h, p, :] <- rotated k;  v_cache[b, h, p, :] <- v   (cache_strides =
+ *          element strides of batch, head and position; the last dim contiguous).
+ *   Rotation with c = cos_tab[p, i], s = sin_tab[p, i] (fp32, (positions, hd/2)):
+ *   out[i] = x[i]*c - x[i+hd/2]*s,  out[i+hd/2] = x[i+hd/2]*c + x[i]*s. */
+int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,
+               const float* cos_tab, const float* sin_tab, int64_t p0, const int64_t* pos,
+               void* q_out, void* k_cache, void* v_cache, const int64_t cache_strides[3],
+               int dtype, void* stream);
+
+/* SwiGLU: gu (M, 2I) holds [gate | up] per row; out (M, I) = silu(gate) * up with silu
+ * rounded to the storage type before the product, as silu(g) * u in two steps. */
+int bi_swiglu(const void* gu, void* out, int64_t M, int64_t I, int dtype, void* stream);
+
 /* Static description of a status code. */
 const char* bi_status_string(int status);
 

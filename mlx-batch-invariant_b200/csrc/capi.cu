@@ -372,6 +372,43 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
                            beta, dtype, flags, rank, world, epoch, stream);
 }
 
+int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,
+               const float* cos_tab, const float* sin_tab, int64_t p0, const int64_t* pos,
+               void* q_out, void* k_cache, void* v_cache, const int64_t cache_strides[3],
+               int dtype, void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
+  }
+  if (B < 0 || L < 0 || hq < 0 || hk < 0 || hd <= 0 || hd % 2 != 0 || p0 < 0) {
+    return set_error(BI_ERR_INVALID, "bad rope sizes (hd must be even and positive)");
+  }
+  if (B * L * (hq + hk) > 0 &&
+      (qkv == nullptr || cos_tab == nullptr || sin_tab == nullptr || cache_strides == nullptr ||
+       (hq > 0 && q_out == nullptr) || (hk > 0 && (k_cache == nullptr || v_cache == nullptr)))) {
+    return set_error(BI_ERR_INVALID, "null pointer");
+  }
+  int st = check_device();
+  if (st) return st;
+  RopeArgs a{qkv, B, L, hq, hk, hd, cos_tab, sin_tab, p0, pos, q_out, k_cache, v_cache,
+             cache_strides != nullptr ? cache_strides[0] : 0,
+             cache_strides != nullptr ? cache_strides[1] : 0,
+             cache_strides != nullptr ? cache_strides[2] : 0};
+  return launch_rope_kv(a, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int bi_swiglu(const void* gu, void* out, int64_t M, int64_t I, int dtype, void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
+  }
+  if (M < 0 || I < 0) return set_error(BI_ERR_INVALID, "negative size");
+  if (M * I > 0 && (gu == nullptr || out == nullptr)) return set_error(BI_ERR_INVALID, "null pointer");
+  int st = check_device();
+  if (st) return st;
+  return launch_swiglu(gu, out, M, I, dtype, static_cast<cudaStream_t>(stream));
+}
+
 const char* bi_status_string(int status) {
   switch (status) {
     case BI_OK: return "ok";

@@ -77,6 +77,23 @@ constexpr int kSimtBK = 8;
 int encode_tiled16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides, const uint32_t* box, int dtype);
 
+// Decoder-harness elementwise steps (harness.cu).
+struct RopeArgs {
+  const void* qkv;         // (B, L, (hq + 2 hk) * hd): q heads, k heads, v heads
+  int64_t B, L, hq, hk, hd;
+  const float* cos_tab;    // (positions, hd / 2)
+  const float* sin_tab;
+  int64_t p0;
+  const int64_t* pos;      // nullable: row l sits at position (pos ? *pos : p0) + l
+  void* q_out;             // (B, hq, L, hd)
+  void* k_cache;
+  void* v_cache;
+  int64_t cs0, cs1, cs2;   // cache strides (elements) of batch, head, position
+};
+int launch_rope_kv(const RopeArgs& a, int dtype, cudaStream_t stream);
+int launch_swiglu(const void* gu, void* out, int64_t M, int64_t I, int dtype,
+                  cudaStream_t stream);
+
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
 // g.out points at column cols[rank] of the output whose first column is out_base.
 int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, void* out_base,

@@ -21,9 +21,11 @@ value is ever summed across GPUs and the logits are also bitwise those of one GP
 * gate/up: rank r holds rows shard_bounds(inter, g)[r] of both, applies SwiGLU to its
   slice and all-gathers the activation before down_proj.
 
-RMSNorm, SiLU, RoPE, the embedding lookup and the residual adds are stock PyTorch ops
-run on replicated rows; each computes every output element on its own, so they are
-batch-invariant on B200 (tests/test_mode_gpu.py guards that).
+RMSNorm, the embedding lookup and the residual adds are stock PyTorch ops run on
+replicated rows; RoPE with the KV-cache write, and SwiGLU, are two fused libbi.so
+kernels (bi_rope_kv, bi_swiglu) on CUDA and the equivalent torch expressions on CPU.
+Each computes every output element on its own, so all are batch-invariant on B200
+(tests/test_mode_gpu.py and tests/test_decoder_gpu.py guard that).
 """
 
 import dataclasses
@@ -34,7 +36,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from . import parallel
+from . import _lib, parallel
 from ._attention import scaled_dot_product_attention
 
 
@@ -175,6 +177,31 @@ class Decoder:
             return self._fused[key].linear(x, w_shard)
         return self._gather(F.linear(x, w_shard), n_total)
 
+    def _rope_kv(self, qkv, B, L, li, pos):
+        """libbi.so bi_rope_kv: rotated q (B, hq, L, hd), and the rotated k / the v of the
+        L new rows written into layer li's cache at position (pos or self.pos) + l."""
+        hd = self.cfg.head_dim
+        q = torch.empty((B, self.hq, L, hd), dtype=self.dtype, device=self.device)
+        qkv = qkv.contiguous()
+        ck, cv = self.cache_k[li], self.cache_v[li]
+        st = _lib.lib().bi_rope_kv(
+            qkv.data_ptr(), B, L, self.hq, self.hk, hd, self.cos.data_ptr(), self.sin.data_ptr(),
+            self.pos if pos is None else 0, pos.data_ptr() if pos is not None else None,
+            q.data_ptr(), ck.data_ptr(), cv.data_ptr(), _lib.i64_3(ck.stride()[:3]),
+            _lib.dtype_code(self.dtype), _lib.stream_handle(self.device))
+        _lib.check(st, "bi_rope_kv")
+        return q
+
+    def _swiglu(self, gu):
+        """libbi.so bi_swiglu: silu(gate) * up of a [gate | up] projection."""
+        lead, width = gu.shape[:-1], gu.shape[-1]
+        g2 = gu.reshape(-1, width).contiguous()
+        out = torch.empty((g2.shape[0], width // 2), dtype=self.dtype, device=self.device)
+        _lib.check(_lib.lib().bi_swiglu(g2.data_ptr(), out.data_ptr(), g2.shape[0], width // 2,
+                                        _lib.dtype_code(self.dtype),
+                                        _lib.stream_handle(self.device)), "bi_swiglu")
+        return out.reshape(*lead, width // 2)
+
     def _attention(self, q, k, v, L, mask=None):
         from . import is_enabled
         if is_enabled():
@@ -211,27 +238,39 @@ class Decoder:
         else:
             p0, mask = self.pos, None
             cos, sin = self.cos[p0:p0 + L], self.sin[p0:p0 + L]
+        native = self.device.type == "cuda"  # fused kernels; CPU runs keep the torch ops
         x = F.embedding(ids, self.embed)
         for li, p in enumerate(self.layers):
             y = F.rms_norm(x, (d,), p["n1"], cfg.eps)
-            q, k, v = F.linear(y, p["wqkv"]).split((hq * hd, hk * hd, hk * hd), dim=-1)
-            q = _rope(q.reshape(B, L, hq, hd).transpose(1, 2), cos, sin)
-            k = _rope(k.reshape(B, L, hk, hd).transpose(1, 2), cos, sin)
-            v = v.reshape(B, L, hk, hd).transpose(1, 2)
+            qkv = F.linear(y, p["wqkv"])
             ck, cv = self.cache_k[li][:B], self.cache_v[li][:B]
+            if native:
+                q = self._rope_kv(qkv, B, L, li, pos)
+            else:
+                q, k, v = qkv.split((hq * hd, hk * hd, hk * hd), dim=-1)
+                q = _rope(q.reshape(B, L, hq, hd).transpose(1, 2), cos, sin)
+                k = _rope(k.reshape(B, L, hk, hd).transpose(1, 2), cos, sin)
+                v = v.reshape(B, L, hk, hd).transpose(1, 2)
+                if static:
+                    ck.index_copy_(2, pos, k)
+                    cv.index_copy_(2, pos, v)
+                else:
+                    ck[:, :, p0:p0 + L] = k
+                    cv[:, :, p0:p0 + L] = v
             if static:
-                ck.index_copy_(2, pos, k)
-                cv.index_copy_(2, pos, v)
                 a = self._attention(q, ck, cv, 1, mask)
             else:
-                ck[:, :, p0:p0 + L] = k
-                cv[:, :, p0:p0 + L] = v
                 a = self._attention(q, ck[:, :, :p0 + L], cv[:, :, :p0 + L], L)
             a = self._gather(a.transpose(1, 2).reshape(B, L, hq * hd), cfg.heads * hd)
             x = x + self._column(a, p["wo"], d, d)
             y = F.rms_norm(x, (d,), p["n2"], cfg.eps)
-            gate, up = F.linear(y, p["wgu"]).split((self.inter_local, self.inter_local), dim=-1)
-            act = self._gather(F.silu(gate) * up, cfg.inter)
+            gu = F.linear(y, p["wgu"])
+            if native:
+                act = self._swiglu(gu)
+            else:
+                gate, up = gu.split((self.inter_local, self.inter_local), dim=-1)
+                act = F.silu(gate) * up
+            act = self._gather(act, cfg.inter)
             x = x + self._column(act, p["wd"], d, d)
         if not static:
             self.pos += L

@@ -78,3 +78,50 @@ def test_graph_decode_matches_eager_decode_bitwise(model):
         g1 = dec.DecodeGraph(model, 1)
         logits1, _, _ = dec.generate(model, ids[:1], 6, g1)
         assert dec.differing(dec.slot0_bits(logits1), eager) == [0] * eager.shape[0]
+
+
+def test_fused_rope_and_cache_write_match_the_torch_expression_bitwise():
+    """bi_rope_kv against the decoder's torch RoPE (fp32 ops, then bf16) and plain cache
+    writes, with the position given on the host and as a device tensor."""
+    from mlx_batch_invariant_b200 import _lib
+    from mlx_batch_invariant_b200.decoder import _rope
+    B, L, hq, hk, hd, P, p0 = 3, 5, 4, 2, 64, 32, 7
+    g = torch.Generator(device="cuda").manual_seed(9)
+    qkv = torch.randn(B, L, (hq + 2 * hk) * hd, generator=g, device="cuda").to(torch.bfloat16)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, hd, 2, device="cuda", dtype=torch.float32) / hd))
+    ang = torch.arange(P, device="cuda", dtype=torch.float32)[:, None] * inv[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    q, k, v = qkv.split((hq * hd, hk * hd, hk * hd), dim=-1)
+    want_q = _rope(q.reshape(B, L, hq, hd).transpose(1, 2), cos[p0:p0 + L], sin[p0:p0 + L])
+    want_k = _rope(k.reshape(B, L, hk, hd).transpose(1, 2), cos[p0:p0 + L], sin[p0:p0 + L])
+    want_v = v.reshape(B, L, hk, hd).transpose(1, 2)
+    for pos in (None, torch.tensor([p0], device="cuda")):
+        q_out = torch.empty(B, hq, L, hd, dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros(B, hk, P, hd, dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        _lib.check(_lib.lib().bi_rope_kv(
+            qkv.data_ptr(), B, L, hq, hk, hd, cos.data_ptr(), sin.data_ptr(),
+            p0 if pos is None else 0, pos.data_ptr() if pos is not None else None,
+            q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), _lib.i64_3(kc.stride()[:3]),
+            _lib.BI_BF16, torch.cuda.current_stream().cuda_stream), "bi_rope_kv")
+        torch.cuda.synchronize()
+        assert torch.equal(q_out.view(torch.int16), want_q.contiguous().view(torch.int16))
+        assert torch.equal(kc[:, :, p0:p0 + L].view(torch.int16), want_k.contiguous().view(torch.int16))
+        assert torch.equal(vc[:, :, p0:p0 + L], want_v)
+        assert not kc[:, :, :p0].any() and not kc[:, :, p0 + L:].any()
+
+
+def test_fused_swiglu_is_within_one_ulp_of_torch():
+    from mlx_batch_invariant_b200 import _lib
+    M, I = 37, 1024
+    g = torch.Generator(device="cuda").manual_seed(10)
+    gu = (torch.randn(M, 2 * I, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    out = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    _lib.check(_lib.lib().bi_swiglu(gu.data_ptr(), out.data_ptr(), M, I, _lib.BI_BF16,
+                                    torch.cuda.current_stream().cuda_stream), "bi_swiglu")
+    want = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    torch.cuda.synchronize()
+    a = out.float()
+    w = want.float()
+    ulp = torch.clamp(w.abs(), min=2.0 ** -126) * 2.0 ** -7
+    assert ((a - w).abs() <= ulp).all()
