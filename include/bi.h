@@ -241,7 +241,9 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
  *   k_cache[b, h, p, :] <- rotated k;  v_cache[b, h, p, :] <- v   (cache_strides =
  *          element strides of batch, head and position; the last dim contiguous).
  *   Rotation with c = cos_tab[p, i], s = sin_tab[p, i] (fp32, (positions, hd/2)):
- *   out[i] = x[i]*c - x[i+hd/2]*s,  out[i+hd/2] = x[i+hd/2]*c + x[i]*s. */
+ *   out[i] = x[i]*c - x[i+hd/2]*s,  out[i+hd/2] = x[i+hd/2]*c + x[i]*s.
+ *   The caller guarantees every p is below both the table's and the caches' length:
+ *   with `pos` in device memory the library cannot see it. */
 int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,
                const float* cos_tab, const float* sin_tab, int64_t p0, const int64_t* pos,
                void* q_out, void* k_cache, void* v_cache, const int64_t cache_strides[3],

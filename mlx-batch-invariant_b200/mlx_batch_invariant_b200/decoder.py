@@ -323,10 +323,20 @@ class DecodeGraph:
         """Continue from host position `pos` with tokens tok (B,) (device tensors)."""
         self.tok.copy_(tok.reshape(self.batch, 1))
         self.pos.fill_(pos)
+        self._next = pos  # host copy of the position the next replay writes
 
     def step(self):
-        """One decode step; returns the graph's logits buffer (overwritten by the next)."""
+        """One decode step; returns the graph's logits buffer (overwritten by the next).
+        Refuses to run past the end of the static cache (the replay's position lives on
+        the device, where nothing else would stop it)."""
+        nxt = getattr(self, "_next", None)
+        if nxt is None:
+            raise RuntimeError("DecodeGraph.start() must come before step()")
+        if nxt >= self.model.max_len:
+            raise ValueError("decode position %d is past the cache length %d"
+                             % (nxt, self.model.max_len))
         self.graph.replay()
+        self._next = nxt + 1
         return self.logits
 
 

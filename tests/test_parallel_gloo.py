@@ -271,3 +271,23 @@ def test_decoder_static_step_matches_eager_decode_on_cpu():
     assert pos.item() == 10 and model.pos == 6
     np.testing.assert_allclose(static.numpy(), eager.numpy(), rtol=1e-5, atol=1e-6)
     assert np.array_equal(static.argmax(-1).numpy(), eager.argmax(-1).numpy())
+
+
+def test_decode_graph_refuses_to_step_past_the_cache():
+    """The host guard of DecodeGraph.step (no CUDA needed to reach it)."""
+    _setup_paths()
+    from mlx_batch_invariant_b200 import decoder as dec
+
+    class _Fake:  # a DecodeGraph without a captured graph
+        pass
+    g = _Fake()
+    g.model = type("M", (), {"max_len": 5})()
+    g.graph = type("G", (), {"replay": staticmethod(lambda: None)})()
+    g.logits = "logits"
+    step = dec.DecodeGraph.step.__get__(g)
+    with pytest.raises(RuntimeError):
+        step()
+    g._next = 4
+    assert step() == "logits" and g._next == 5
+    with pytest.raises(ValueError):
+        step()
