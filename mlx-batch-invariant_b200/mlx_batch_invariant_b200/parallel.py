@@ -181,17 +181,25 @@ class FusedColumnParallel:
         _lib.check(L.bi_peer_alloc(self._stage_bytes + _lib.PEER_FLAG_BYTES, ctypes.byref(ptr),
                                    handle), "bi_peer_alloc")
         self._local = ptr.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
         self._ptrs, self._opened = [], []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                self._ptrs.append(self._local)
-                continue
-            q = ctypes.c_void_p()
-            _lib.check(L.bi_peer_open(h, ctypes.byref(q)), "bi_peer_open")
-            self._ptrs.append(q.value)
-            self._opened.append(q.value)
+        try:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self._ptrs.append(self._local)
+                    continue
+                q = ctypes.c_void_p()
+                _lib.check(L.bi_peer_open(h, ctypes.byref(q)), "bi_peer_open")
+                self._ptrs.append(q.value)
+                self._opened.append(q.value)
+        except BaseException:
+            # release what this rank holds; its peers fail on their next exchange
+            for q in self._opened:
+                L.bi_peer_close(q)
+            L.bi_peer_free(self._local)
+            self._local, self._opened = None, []
+            raise
         self._stages = (ctypes.c_void_p * self.world)(*self._ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*[p + self._stage_bytes for p in self._ptrs])
 
