@@ -491,13 +491,19 @@ constexpr int R = 4;                 // keys per partial per stage
 constexpr int KEYS = PARTIALS * R;   // keys per stage
 constexpr int BOX_D = 64;            // columns per TMA box (128-byte rows)
 
+// Two CTAs per SM (128 registers, ~66 KB each): one 128-key stage of K and V per CTA
+// at D = 128 (two at D = 64), the other CTA's stages covering this one's latency.  The
+// region before the barriers holds the stage ring, and after the walk the combine's
+// partials (up to 4 heads x 32 partials x D floats, their m / l and denominators).
 template <int D>
 struct Plan {
   static constexpr int BOXES = D / BOX_D;
   static constexpr int TSB = KEYS * D * 2;               // one tensor's stage bytes
-  static constexpr int STAGES = D == 128 ? 3 : 4;
-  static constexpr int SMEM = 1024 + 2 * STAGES * TSB + STAGES * 8 + 64;
-  static_assert(SMEM <= 227 * 1024, "shared memory above the per-CTA limit");
+  static constexpr int STAGES = D == 128 ? 1 : 2;
+  static constexpr int COMB = 4 * PARTIALS * D * 4 + 2 * 4 * PARTIALS * 4 + 64;
+  static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
+  static constexpr int SMEM = 1024 + REGION + STAGES * 8 + 64;
+  static_assert(2 * SMEM <= 227 * 1024, "two CTAs per SM must fit");
 };
 
 template <typename T>
@@ -562,7 +568,7 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
 }
 
 template <typename T, int D, int GH>
-__global__ void __launch_bounds__(64 * GH, 1)
+__global__ void __launch_bounds__(64 * GH, 2)
     sdpa_mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const Params p) {
   using PL = Plan<D>;
@@ -581,7 +587,7 @@ __global__ void __launch_bounds__(64 * GH, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + STAGES * TSB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * STAGES * TSB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PL::REGION);
   int* done_count = reinterpret_cast<int*>(full + STAGES);
   int* issued_count = done_count + STAGES;
   volatile int* abort_flag = issued_count + 1;
