@@ -80,7 +80,7 @@ int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb,
 /*
  * The kernel route and CTA tile bi_gemm uses for (dtype, K, N, layout).  The result
  * never depends on M; this is the library's analogue of the reference's public
- * TILE constant (_gemm.py:172-174).  Any out-pointer may be null.
+ * TILE constant (_gemm.py:27).  Any out-pointer may be null.
  */
 int bi_gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk,
                   int* route, int* bm, int* bn, int* bk);
@@ -201,8 +201,12 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
  * bi_gemm_allgather, and it calls no cudaMalloc, cudaFree or other allocating routine.
  *
  *   devices[r]  the CUDA device ordinal rank r runs on, all in THIS process (one
- *               process drives every rank, with peer access enabled between them);
- *               stages[r] must be addressable from each of these devices.
+ *               process drives every rank), one rank per device: a repeated ordinal
+ *               is rejected (BI_ERR_INVALID), and so is a call whose devices[rank]
+ *               is not the current device.  The call enables peer access from the
+ *               current device to every other rank's device (already enabled counts
+ *               as success) and returns BI_ERR_UNSUPPORTED where the hardware has
+ *               none; stages[r] must be addressable from each of these devices.
  *   world       at most BI_MAX_PEERS; larger values are rejected (BI_ERR_INVALID)
  *               because the static block holds flags for BI_MAX_PEERS ranks.
  *
@@ -242,12 +246,14 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
  *          element strides of batch, head and position; the last dim contiguous).
  *   Rotation with c = cos_tab[p, i], s = sin_tab[p, i] (fp32, (positions, hd/2)):
  *   out[i] = x[i]*c - x[i+hd/2]*s,  out[i+hd/2] = x[i+hd/2]*c + x[i]*s.
- *   The caller guarantees every p is below both the table's and the caches' length:
- *   with `pos` in device memory the library cannot see it. */
+ *   n_pos  the positions both tables and both caches hold.  With pos == NULL the call
+ *          checks p0 + L <= n_pos (else BI_ERR_INVALID).  With a device `pos` the kernel
+ *          writes no row whose position falls outside [0, n_pos) and records site 1,
+ *          reason 2 (tagged bit 17) in the device error word (bi_device_error). */
 int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,
                const float* cos_tab, const float* sin_tab, int64_t p0, const int64_t* pos,
-               void* q_out, void* k_cache, void* v_cache, const int64_t cache_strides[3],
-               int dtype, void* stream);
+               int64_t n_pos, void* q_out, void* k_cache, void* v_cache,
+               const int64_t cache_strides[3], int dtype, void* stream);
 
 /* SwiGLU: gu (M, 2I) holds [gate | up] per row; out (M, I) = silu(gate) * up with silu
  * rounded to the storage type before the product, as silu(g) * u in two steps. */

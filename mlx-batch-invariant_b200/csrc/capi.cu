@@ -6,6 +6,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "internal.h"
 
@@ -74,6 +75,33 @@ static int gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk) {
   if (K <= 0 || K % 8 != 0) return BI_ROUTE_SIMT;
   if (!b_is_nk && N % 8 != 0) return BI_ROUTE_SIMT;
   return BI_ROUTE_TCGEN05;
+}
+
+// Peer access from device `cur` (current) to `peer`'s memory, enabled if the hardware
+// allows it; "already enabled" counts as success.  A pair found usable is remembered.
+static int ensure_peer_access(int cur, int peer) {
+  static std::mutex mu;
+  static bool ok[kMaxDevices][kMaxDevices] = {};
+  if (cur < 0 || cur >= kMaxDevices || peer < 0 || peer >= kMaxDevices) {
+    return set_error(BI_ERR_INVALID, "device ordinal %d out of range", cur < 0 ? cur : peer);
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (ok[cur][peer]) return BI_OK;
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, cur, peer);
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceCanAccessPeer");
+  if (!can) {
+    return set_error(BI_ERR_UNSUPPORTED, "device %d cannot access device %d's memory (no peer "
+                     "access between them)", cur, peer);
+  }
+  e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();  // the answer is success; do not leave it as the last error
+  } else if (e != cudaSuccess) {
+    return cuda_status(e, "cudaDeviceEnablePeerAccess");
+  }
+  ok[cur][peer] = true;
+  return BI_OK;
 }
 
 static int check_device() {
@@ -356,13 +384,42 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
                      world, BI_MAX_PEERS, BI_MAX_PEERS);
   }
   if (devices == nullptr) return set_error(BI_ERR_INVALID, "devices is null");
+  if (rank < 0 || rank >= world) return set_error(BI_ERR_INVALID, "rank outside [0, world)");
+  // One rank per device: two ranks on one device would share its block (the CTA counter
+  // and the flags), and one rank's counter reset could land in the other's call.
+  for (int r = 0; r < world; ++r) {
+    for (int r2 = r + 1; r2 < world; ++r2) {
+      if (devices[r] == devices[r2]) {
+        return set_error(BI_ERR_INVALID,
+                         "bi_gemm_allgather_static: ranks %d and %d are both on device %d; "
+                         "the static flag block holds one rank per device",
+                         r, r2, devices[r]);
+      }
+    }
+  }
+  int st = check_device();
+  if (st) return st;
+  // The local GEMM counts its CTAs in the block of the device it runs on.
+  const int cur = current_device();
+  if (devices[rank] != cur) {
+    return set_error(BI_ERR_INVALID,
+                     "bi_gemm_allgather_static: devices[%d] = %d but device %d is current; "
+                     "call each rank with its own device current",
+                     rank, devices[rank], cur);
+  }
+  // The kernels store into every other rank's block and staging area: this device must
+  // reach each of those devices' memory.
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    st = ensure_peer_access(cur, devices[r]);
+    if (st) return st;
+  }
   // Each rank's flag block is its device's copy of the library's static array.
   void* flags[BI_MAX_PEERS] = {};
   for (int r = 0; r < world; ++r) {
-    const int st = static_flag_block(devices[r], &flags[r]);
+    st = static_flag_block(devices[r], &flags[r]);
     if (st) return st;
   }
-  if (rank < 0 || rank >= world) return set_error(BI_ERR_INVALID, "rank outside [0, world)");
   // The block keeps the previous call's contents; the CTA counter must start at zero.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(static_cast<uint32_t*>(flags[rank]) + kFlagCounter, 0,
@@ -374,8 +431,8 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
 
 int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,
                const float* cos_tab, const float* sin_tab, int64_t p0, const int64_t* pos,
-               void* q_out, void* k_cache, void* v_cache, const int64_t cache_strides[3],
-               int dtype, void* stream) {
+               int64_t n_pos, void* q_out, void* k_cache, void* v_cache,
+               const int64_t cache_strides[3], int dtype, void* stream) {
   g_msg[0] = '\0';
   if (dtype != BI_F32 && dtype != BI_F16 && dtype != BI_BF16) {
     return set_error(BI_ERR_INVALID, "unknown dtype %d", dtype);
@@ -388,9 +445,15 @@ int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, in
        (hq > 0 && q_out == nullptr) || (hk > 0 && (k_cache == nullptr || v_cache == nullptr)))) {
     return set_error(BI_ERR_INVALID, "null pointer");
   }
+  if (n_pos < 0) return set_error(BI_ERR_INVALID, "n_pos must not be negative");
+  if (pos == nullptr && p0 + L > n_pos) {
+    return set_error(BI_ERR_INVALID, "positions %lld..%lld are past the %lld the tables hold",
+                     static_cast<long long>(p0), static_cast<long long>(p0 + L - 1),
+                     static_cast<long long>(n_pos));
+  }
   int st = check_device();
   if (st) return st;
-  RopeArgs a{qkv, B, L, hq, hk, hd, cos_tab, sin_tab, p0, pos, q_out, k_cache, v_cache,
+  RopeArgs a{qkv, B, L, hq, hk, hd, cos_tab, sin_tab, p0, pos, n_pos, q_out, k_cache, v_cache,
              cache_strides != nullptr ? cache_strides[0] : 0,
              cache_strides != nullptr ? cache_strides[1] : 0,
              cache_strides != nullptr ? cache_strides[2] : 0};
@@ -429,7 +492,9 @@ int bi_device_error(int clear) {
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
   unsigned w = read_error_gemm_tc(clear != 0);
   const unsigned s = read_error_sdpa(clear != 0);
+  const unsigned h = read_error_harness(clear != 0);
   if (w == 0 && s != 0) w = s | (1u << 16);  // sdpa sites are tagged in bit 16
+  if (w == 0 && h != 0) w = h | (1u << 17);  // decoder-harness sites in bit 17
   return static_cast<int>(w);
 }
 

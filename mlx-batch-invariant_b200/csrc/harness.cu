@@ -15,6 +15,13 @@
 namespace bi {
 namespace harness {
 
+// Error site of the rope kernel: a row whose position lies outside [0, n_pos) (the
+// position can come from device memory, where the host cannot check it).
+constexpr unsigned kSiteRopePosition = 1;
+constexpr unsigned kErrReasonRange = 2;
+
+__device__ unsigned g_error_word = 0;
+
 template <typename T>
 __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
   const int64_t half = a.hd / 2;
@@ -22,6 +29,13 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
   const int64_t total = a.B * a.L * nheads * half;
   const T* qkv = static_cast<const T*>(a.qkv);
   const int64_t base = a.pos != nullptr ? *a.pos : a.p0;
+  // Rows past the tables or the caches are not written; the call reports it through
+  // the device error word instead.
+  if (base < 0 || base + a.L > a.n_pos) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      record_error(&g_error_word, (kSiteRopePosition << 8) | kErrReasonRange);
+    }
+  }
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t i = idx % half;
@@ -31,6 +45,7 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
     const int64_t l = t % a.L;
     const int64_t b = t / a.L;
     const int64_t pos = base + l;
+    if (pos < 0 || pos >= a.n_pos) continue;
     const T* src = qkv + ((b * a.L + l) * nheads + h) * a.hd;
     if (h < a.hq + a.hk) {
       const float c = a.cos_tab[pos * half + i];
@@ -123,6 +138,16 @@ static int launch_swiglu_t(const void* gu, void* out, int64_t M, int64_t I, cuda
   }
   harness::swiglu_kernel<T, false><<<harness::grid_for(M * I), 256, 0, stream>>>(g, o, M, I);
   return cuda_status(cudaGetLastError(), "swiglu launch");
+}
+
+unsigned read_error_harness(bool clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, harness::g_error_word, sizeof(v));
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(harness::g_error_word, &z, sizeof(z));
+  }
+  return v;
 }
 
 int launch_swiglu(const void* gu, void* out, int64_t M, int64_t I, int dtype,

@@ -85,6 +85,7 @@ struct RopeArgs {
   const float* sin_tab;
   int64_t p0;
   const int64_t* pos;      // nullable: row l sits at position (pos ? *pos : p0) + l
+  int64_t n_pos;           // positions the tables and the caches hold
   void* q_out;             // (B, hq, L, hd)
   void* k_cache;
   void* v_cache;
@@ -106,6 +107,7 @@ int launch_sdpa(const SdpaArgs& s, cudaStream_t stream);
 // Device error words, one per translation unit; read and optionally clear.
 unsigned read_error_gemm_tc(bool clear);
 unsigned read_error_sdpa(bool clear);
+unsigned read_error_harness(bool clear);
 
 // Per-thread message for bi_last_error().
 int set_error(int status, const char* fmt, ...);

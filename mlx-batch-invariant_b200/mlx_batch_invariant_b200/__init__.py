@@ -159,8 +159,8 @@ def batch_invariant_mode(strict=True):
         if D % 32 or V % 32 or D != V or D > MAX_HEAD_DIM or Hkv == 0 or H % Hkv:
             return stock()
         if H != Hkv and not enable_gqa:
-            return saved["sdpa"](query, key, value, attn_mask=attn_mask, dropout_p=dropout_p,
-                                 is_causal=is_causal, scale=scale, enable_gqa=enable_gqa)
+            # stock torch broadcasts a single KV head here; that call is not invariant
+            return stock()
         if attn_mask is not None and is_causal:
             return stock()
         if attn_mask is not None and not (isinstance(attn_mask, torch.Tensor)

@@ -13,7 +13,7 @@ import torch
 from . import _lib
 
 # The tensor-core tile used for float16 / bfloat16: fixed for every shape and every
-# M (cf. the reference's TILE, _gemm.py:172-174).  UMMA_* is the tcgen05 instruction.
+# M (cf. the reference's TILE, _gemm.py:27).  UMMA_* is the tcgen05 instruction.
 TILE = dict(BM=128, BN=256, BK=64, UMMA_M=128, UMMA_N=256, UMMA_K=16)
 # The CUDA-core tile (float32, and float16/bfloat16 when K % 8 != 0).
 SIMT_TILE = dict(BM=128, BN=128, BK=8)

@@ -79,8 +79,8 @@ def _bind(lib):
     lib.bi_gemm_allgather_static.restype = ctypes.c_int
     lib.bi_gemm_allgather_static.argtypes = gather + [ctypes.POINTER(ctypes.c_int)] + tail
     lib.bi_rope_kv.restype = ctypes.c_int
-    lib.bi_rope_kv.argtypes = [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp,
-                               _vp, _i64_3, ctypes.c_int, _vp]
+    lib.bi_rope_kv.argtypes = [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64,
+                               _vp, _vp, _vp, _i64_3, ctypes.c_int, _vp]
     lib.bi_swiglu.restype = ctypes.c_int
     lib.bi_swiglu.argtypes = [_vp, _vp, _i64, _i64, ctypes.c_int, _vp]
 

@@ -187,7 +187,7 @@ class Decoder:
         st = _lib.lib().bi_rope_kv(
             qkv.data_ptr(), B, L, self.hq, self.hk, hd, self.cos.data_ptr(), self.sin.data_ptr(),
             self.pos if pos is None else 0, pos.data_ptr() if pos is not None else None,
-            q.data_ptr(), ck.data_ptr(), cv.data_ptr(), _lib.i64_3(ck.stride()[:3]),
+            self.max_len, q.data_ptr(), ck.data_ptr(), cv.data_ptr(), _lib.i64_3(ck.stride()[:3]),
             _lib.dtype_code(self.dtype), _lib.stream_handle(self.device))
         _lib.check(st, "bi_rope_kv")
         return q
@@ -321,6 +321,10 @@ class DecodeGraph:
 
     def start(self, tok, pos):
         """Continue from host position `pos` with tokens tok (B,) (device tensors)."""
+        pos = int(pos)
+        if not 0 <= pos < self.model.max_len:
+            raise ValueError("decode position %d is outside the cache [0, %d)"
+                             % (pos, self.model.max_len))
         self.tok.copy_(tok.reshape(self.batch, 1))
         self.pos.fill_(pos)
         self._next = pos  # host copy of the position the next replay writes

@@ -14,11 +14,12 @@
  * tests/test_oracle.py, and (2) the committed golden fixtures in tests/golden/.
  *
  * GEMM (mlx_batch_invariant/_gemm.py:29-130): per output element one fp32
- * accumulator, zero-initialised (:198-205).  K is walked in slices of 8, ascending --
- * the k0-then-kk order of 8-deep MMA steps at :209-251 -- and each slice is summed in
+ * accumulator, zero-initialised (:51-58), out-of-range rows and columns
+ * loaded as zero (:63-80).  K is walked in slices of 8, ascending --
+ * the k0-then-kk order of 8-deep MMA steps at :62-104 -- and each slice is summed in
  * order into a fresh fp32 partial, p = fmaf(a[m,k], b[k,n], p), which is then added
  * to the accumulator, acc = acc + p (Apple does not specify the order inside its
- * 8x8x8 fragment; sequential is taken).  Then the epilogue of :265-276,
+ * 8x8x8 fragment; sequential is taken).  Then the epilogue of :118-129,
  * v = alpha*acc + beta*bias with each operation rounded to fp32 (no contraction),
  * rounded once to the output type, round-to-nearest-even.
  *

@@ -3,7 +3,7 @@
     python oracle/build.py [--force]
 
 The reference itself cannot be built or run here: its kernels are Metal Shading
-Language strings launched through MLX (mlx_batch_invariant/_gemm.py:176-304,
+Language strings launched through MLX (mlx_batch_invariant/_gemm.py:29-157,
 _attention.py:32-158), and neither MLX nor Metal exists on Linux.  So there is no
 oracle/_ref/ build; bi_oracle.c restates the reference's algorithm instead.
 """

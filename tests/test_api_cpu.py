@@ -231,3 +231,26 @@ def test_fused_allgather_validates_its_partition_before_touching_a_device():
     assert _gather_call(L, [0] * 10, world=9) == -1            # above BI_MAX_PEERS
     assert _gather_call(L, [0, 16, 32], ldo=24) == -3          # ldo < cols[world]
     assert _gather_call(L, [0, 16, 32], dtype=_lib.BI_F32) == -2  # tensor-core dtypes only
+
+
+def test_static_allgather_rejects_two_ranks_on_one_device():
+    """bi_gemm_allgather_static keeps one flag block per device, so a device named twice
+    is refused before any CUDA call (no GPU needed)."""
+    L = _lib.lib()
+    devices = (ctypes.c_int * 2)(0, 0)
+    stages = (ctypes.c_void_p * 2)()
+    cols = (ctypes.c_int64 * 3)(0, 8, 16)
+    st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 16, stages, cols, 1, 8, 1,
+                                    1.0, 1.0, _lib.BI_BF16, devices, 0, 2, 1, None)
+    assert st == -1
+    assert b"both on device 0" in L.bi_last_error()
+
+
+def test_static_allgather_rejects_a_rank_outside_the_world():
+    L = _lib.lib()
+    devices = (ctypes.c_int * 2)(0, 1)
+    stages = (ctypes.c_void_p * 2)()
+    cols = (ctypes.c_int64 * 3)(0, 8, 16)
+    st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 16, stages, cols, 1, 8, 1,
+                                    1.0, 1.0, _lib.BI_BF16, devices, 2, 2, 1, None)
+    assert st == -1 and b"rank" in L.bi_last_error()

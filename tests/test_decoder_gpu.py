@@ -101,7 +101,7 @@ def test_fused_rope_and_cache_write_match_the_torch_expression_bitwise():
         vc = torch.zeros_like(kc)
         _lib.check(_lib.lib().bi_rope_kv(
             qkv.data_ptr(), B, L, hq, hk, hd, cos.data_ptr(), sin.data_ptr(),
-            p0 if pos is None else 0, pos.data_ptr() if pos is not None else None,
+            p0 if pos is None else 0, pos.data_ptr() if pos is not None else None, P,
             q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), _lib.i64_3(kc.stride()[:3]),
             _lib.BI_BF16, torch.cuda.current_stream().cuda_stream), "bi_rope_kv")
         torch.cuda.synchronize()
@@ -109,6 +109,38 @@ def test_fused_rope_and_cache_write_match_the_torch_expression_bitwise():
         assert torch.equal(kc[:, :, p0:p0 + L].view(torch.int16), want_k.contiguous().view(torch.int16))
         assert torch.equal(vc[:, :, p0:p0 + L], want_v)
         assert not kc[:, :, :p0].any() and not kc[:, :, p0 + L:].any()
+    assert _lib.device_error() == 0
+
+
+def test_rope_position_past_the_cache_is_refused_not_written():
+    """A position at the cache length: the host form is refused before launch; a device
+    position (which the host cannot see) writes nothing and sets the device error word
+    (site 1, reason 2, tagged bit 17)."""
+    from mlx_batch_invariant_b200 import _lib
+    B, L, hq, hk, hd, P = 2, 1, 4, 2, 64, 16
+    qkv = torch.ones(B, L, (hq + 2 * hk) * hd, dtype=torch.bfloat16, device="cuda")
+    cos = torch.ones(P, hd // 2, device="cuda")
+    sin = torch.zeros(P, hd // 2, device="cuda")
+    q_out = torch.zeros(B, hq, L, hd, dtype=torch.bfloat16, device="cuda")
+    # a guard region after the caches: an unchecked write at position P would land there
+    kc_all = torch.zeros(B, hk, P + 4, hd, dtype=torch.bfloat16, device="cuda")
+    vc_all = torch.zeros_like(kc_all)
+    kc, vc = kc_all[:, :, :P], vc_all[:, :, :P]
+    assert _lib.device_error() == 0
+    with pytest.raises(_lib.LibraryError):
+        _lib.check(_lib.lib().bi_rope_kv(
+            qkv.data_ptr(), B, L, hq, hk, hd, cos.data_ptr(), sin.data_ptr(), P, None, P,
+            q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), _lib.i64_3(kc.stride()[:3]),
+            _lib.BI_BF16, torch.cuda.current_stream().cuda_stream), "bi_rope_kv")
+    pos = torch.tensor([P], device="cuda")
+    _lib.check(_lib.lib().bi_rope_kv(
+        qkv.data_ptr(), B, L, hq, hk, hd, cos.data_ptr(), sin.data_ptr(), 0, pos.data_ptr(), P,
+        q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), _lib.i64_3(kc.stride()[:3]),
+        _lib.BI_BF16, torch.cuda.current_stream().cuda_stream), "bi_rope_kv")
+    torch.cuda.synchronize()
+    assert _lib.device_error() == (1 << 17) | (1 << 8) | 2
+    assert _lib.device_error() == 0  # read-and-clear
+    assert not kc_all.any() and not vc_all.any() and not q_out.any()
 
 
 def test_fused_swiglu_is_within_one_ulp_of_torch():

@@ -100,6 +100,30 @@ def test_unsupported_attention_raises_under_strict_and_falls_back_otherwise(bi):
     assert np.array_equal(bits(y), bits(ref))
 
 
+def test_broadcast_kv_head_without_enable_gqa_raises_under_strict(bi):
+    """Stock SDPA broadcasts a single KV head when enable_gqa is False; that call is not
+    the invariant kernel, so strict mode must refuse it rather than pass it through."""
+    q = randn((1, 8, 2, 64), torch.bfloat16, 64, "cuda")
+    k = randn((1, 1, 128, 64), torch.bfloat16, 65, "cuda")
+    v = randn((1, 1, 128, 64), torch.bfloat16, 66, "cuda")
+    with bi.batch_invariant_mode(strict=True):
+        with pytest.raises(NotImplementedError):
+            F.scaled_dot_product_attention(q, k, v)
+        # the same heads with enable_gqa take the kernel
+        y = F.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+    assert np.array_equal(bits(y), bits(bi.scaled_dot_product_attention(q, k, v)))
+    try:
+        ref = F.scaled_dot_product_attention(q, k, v)
+    except RuntimeError:  # a stock backend that refuses the broadcast: same under the mode
+        with bi.batch_invariant_mode(strict=False):
+            with pytest.raises(RuntimeError):
+                F.scaled_dot_product_attention(q, k, v)
+        return
+    with bi.batch_invariant_mode(strict=False):
+        y = F.scaled_dot_product_attention(q, k, v)
+    assert np.array_equal(bits(y), bits(ref))
+
+
 def test_graph_capture_of_a_model_under_the_mode(bi):
     torch.manual_seed(3)
     net = torch.nn.Sequential(torch.nn.Linear(1024, 2048), torch.nn.SiLU(),
