@@ -170,11 +170,28 @@ void oracle_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, const v
  * row-contiguous.  lanes: threads a key row is split over (a power of two dividing
  * D, leaving an even count per lane); D == V.
  */
+void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
+                    const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
+                    int mask_mode, int64_t causal_offset, const void* sinks, float scale,
+                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt,
+                    void* out, const int64_t* os, int out_dt, int lanes, int nthreads);
+
 void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                  const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
                  int mask_mode, int64_t causal_offset, const void* sinks, float scale, int64_t B,
                  int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt, void* out,
                  const int64_t* os, int lanes, int nthreads) {
+  oracle_sdpa_ex(q, qs, k, ks, v, vs, mask, ms, mask_mode, causal_offset, sinks, scale, B, H,
+                 Hkv, qL, N, D, dt, out, os, dt, lanes, nthreads);
+}
+
+/* As oracle_sdpa, with the output written as out_dt: OR_F32 keeps the fold's fp32
+ * result before the final rounding to the input type (for elementwise error bars). */
+void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
+                    const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
+                    int mask_mode, int64_t causal_offset, const void* sinks, float scale,
+                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt,
+                    void* out, const int64_t* os, int out_dt, int lanes, int nthreads) {
   const int64_t G = H / Hkv;
   const int64_t E = D / lanes;
   /* a lane's share of a row: vectors of W bytes (16, 8 or 4, whichever divides its
@@ -272,7 +289,7 @@ void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t*
         float acc = 0.0f;
         for (int p = 0; p < PARTIALS; ++p) acc = fmaf(o[p * D + j], fp[p], acc);
         const float res = lsum == 0.0f ? acc : acc / lsum;
-        store_elem(out, b * os[0] + h * os[1] + s * os[2] + j, res, dt);
+        store_elem(out, b * os[0] + h * os[1] + s * os[2] + j, res, out_dt);
       }
     }
     free(qv);

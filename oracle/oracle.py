@@ -52,6 +52,11 @@ def lib():
         L.oracle_sdpa.argtypes = [vp, _i64p, vp, _i64p, vp, _i64p, vp, _i64p, ctypes.c_int, i64,
                                   vp, ctypes.c_float, i64, i64, i64, i64, i64, i64, ctypes.c_int,
                                   vp, _i64p, ctypes.c_int, ctypes.c_int]
+        L.oracle_sdpa_ex.restype = None
+        L.oracle_sdpa_ex.argtypes = [vp, _i64p, vp, _i64p, vp, _i64p, vp, _i64p, ctypes.c_int,
+                                     i64, vp, ctypes.c_float, i64, i64, i64, i64, i64, i64,
+                                     ctypes.c_int, vp, _i64p, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int]
         L.oracle_round.restype = ctypes.c_float
         L.oracle_round.argtypes = [ctypes.c_float, ctypes.c_int]
         _lib = L
@@ -97,9 +102,10 @@ def lanes_for(D, dtype):
 
 
 def sdpa(q, k, v, mask=None, mask_mode=0, causal_offset=0, sinks=None, scale=None, lanes=None,
-         threads=0):
+         threads=0, out_dtype=None):
     """Host restatement of bi_sdpa.  q (B,H,qL,D), k/v (B,Hkv,N,D); mask is the
-    additive mask (already in q's dtype, 4-D, broadcast dims of size 1) for mode 2."""
+    additive mask (already in q's dtype, 4-D, broadcast dims of size 1) for mode 2.
+    out_dtype=np.float32 returns the fold's fp32 result before the final rounding."""
     q = np.ascontiguousarray(q)
     k = np.ascontiguousarray(k)
     v = np.ascontiguousarray(v)
@@ -111,7 +117,8 @@ def sdpa(q, k, v, mask=None, mask_mode=0, causal_offset=0, sinks=None, scale=Non
         scale = 1.0 / np.sqrt(D)
     if lanes is None:
         lanes = lanes_for(D, dt)
-    out = np.empty((B, H, qL, V), dtype=dt)
+    odt = np.dtype(out_dtype) if out_dtype is not None else dt
+    out = np.empty((B, H, qL, V), dtype=odt)
     ms = [0, 0, 0]
     if mask_mode == 2:
         mask = np.ascontiguousarray(mask.astype(dt))
@@ -124,9 +131,10 @@ def sdpa(q, k, v, mask=None, mask_mode=0, causal_offset=0, sinks=None, scale=Non
     qs = [H * qL * D, qL * D, D]
     ks = [Hkv * N * D, N * D]
     os_ = [H * qL * V, qL * V, V]
-    lib().oracle_sdpa(_ptr(q), _i64s(qs), _ptr(k), _i64s(ks), _ptr(v), _i64s(ks), _ptr(mask),
-                      _i64s(ms), mask_mode, causal_offset, _ptr(sinks), float(scale), B, H, Hkv,
-                      qL, N, D, CODES[dt], _ptr(out), _i64s(os_), lanes, threads)
+    lib().oracle_sdpa_ex(_ptr(q), _i64s(qs), _ptr(k), _i64s(ks), _ptr(v), _i64s(ks),
+                         _ptr(mask), _i64s(ms), mask_mode, causal_offset, _ptr(sinks),
+                         float(scale), B, H, Hkv, qL, N, D, CODES[dt], _ptr(out), _i64s(os_),
+                         CODES[odt], lanes, threads)
     return out
 
 

@@ -57,3 +57,61 @@ def batch_with(ref, pool, B, idx):
         return ref
     parts = ([pool[:idx]] if idx > 0 else []) + [ref] + ([pool[idx + 1:B]] if idx + 1 < B else [])
     return torch.cat(parts)
+
+
+# ---------------------------------------------------------------- attention parity bar
+# Elementwise: the oracle (bi_oracle.c) keeps the fold's fp32 result w before the final
+# rounding to the output type (same inputs, same lane split); each GPU output element
+# must satisfy
+#     |gpu - w| <= 0.5 ulp_T(w) + tau * A_j   (float16 / bfloat16)
+#     |gpu - w| <= 2 ulp_f32(w) + tau * A_j   (float32)
+# with A_j = sum_i p_i |v_ij| / sum_i p_i (float64 weights on |v|), the size of the terms
+# output j sums.  tau = 2^-20 on the CUDA-core route (same fold and order as the oracle;
+# only CUDA's expf and the C library's differ) and 2^-16 on the tensor-core route
+# (score = scale * (q . k) instead of pre-scaled q, visible keys of a stage folded 4 at
+# a time, weights entering P.V as e_hi + e_lo: each moves a weight by a few 2^-19
+# relative at most).
+_MANT = {torch.float16: 10, torch.bfloat16: 7, torch.float32: 23}
+_MIN_NORMAL = {torch.float16: 2.0 ** -14, torch.bfloat16: 2.0 ** -126, torch.float32: 2.0 ** -126}
+
+
+def ulp_of(x, dtype):
+    """Spacing of `dtype` values at |x| (float64 array)."""
+    mag = np.maximum(np.abs(x), _MIN_NORMAL[dtype])
+    return 2.0 ** (np.floor(np.log2(mag)) - _MANT[dtype])
+
+
+def sdpa_tc_route(dtype, H, Hkv, D):
+    """Whether bi_sdpa takes its tensor-core route for these shapes."""
+    return dtype != torch.float32 and (H // Hkv) % 4 == 0 and D in (64, 128)
+
+
+def attn_worst(got, q, k, v, mask_mode=0, mask=None, causal_offset=0, sinks=None):
+    """Largest |gpu - w| / bar over the elements of `got` (see the bar above); <= 1 passes.
+    q (B,H,qL,D), k/v (B,Hkv,N,D) torch tensors; mask the additive mask (4-D, in q's
+    dtype, -inf = masked) for mask_mode 2, or mask_mode 1 with causal_offset."""
+    from oracle import oracle as orc
+    dtype = q.dtype
+    B, H, qL, D = q.shape
+    Hkv, N = k.shape[1], k.shape[2]
+    f32 = lambda t: np.ascontiguousarray(to_np(t).astype(np.float32))
+    q32, k32, v32 = f32(q), f32(k), f32(v)
+    s32 = f32(sinks) if sinks is not None else None
+    m32 = f32(mask) if mask_mode == 2 else None
+    w = orc.sdpa(to_np(q), to_np(k), to_np(v), mask=to_np(mask) if mask_mode == 2 else None,
+                 mask_mode=mask_mode, causal_offset=causal_offset,
+                 sinks=to_np(sinks) if sinks is not None else None, out_dtype=np.float32)
+    m64 = m32
+    if mask_mode == 1:
+        i = np.arange(N)[None, :]
+        s = np.arange(qL)[:, None]
+        m64 = np.where(i <= causal_offset + s, 0.0, -np.inf)[None, None]
+    absv = orc.attention_f64(q32, k32, np.abs(v32), mask=m64, sinks=s32)
+    g = to_np(got).astype(np.float64)
+    w = w.astype(np.float64)
+    tau = 2.0 ** -16 if sdpa_tc_route(dtype, H, Hkv, D) else 2.0 ** -20
+    if dtype == torch.float32:
+        bar = 2 * ulp_of(w, dtype) + tau * absv
+    else:
+        bar = 0.5 * ulp_of(w, dtype) * (1 + 1e-7) + tau * absv
+    return float((np.abs(g - w) / bar).max())

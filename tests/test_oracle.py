@@ -236,3 +236,27 @@ def test_bit_and_ulp_helpers_selftest():
     assert int(orc.ulp_distance(pz[:1], pz[1:], n)[0]) == 0
     pm, n = orc.bits(np.array([np.float32(1e-45), -np.float32(1e-45)], dtype=np.float32))
     assert int(orc.ulp_distance(pm[:1], pm[1:], n)[0]) == 2
+
+
+@pytest.mark.parametrize("dt", ["bfloat16", "float16", "float32"])
+def test_elementwise_attention_bar_accepts_the_rounded_fold(dt):
+    """The GPU tests' elementwise attention bar (conftest.attn_worst) against the oracle's
+    own output rounded to the input type: rounding alone uses at most half an output ulp,
+    so it must pass with room only for the stated tau term."""
+    import torch
+    from conftest import attn_worst, to_np
+    dtype = getattr(torch, dt)
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 8, 3, 128, generator=g).to(dtype)
+    k = torch.randn(1, 2, 300, 128, generator=g).to(dtype)
+    v = torch.randn(1, 2, 300, 128, generator=g).to(dtype)
+    o = orc.sdpa(to_np(q), to_np(k), to_np(v), mask_mode=1, causal_offset=297)
+    if dtype == torch.bfloat16:
+        ot = torch.from_numpy(o.view(np.uint16).astype(np.int32)).to(torch.int16).view(dtype)
+    else:
+        ot = torch.from_numpy(o)
+    assert attn_worst(ot, q, k, v, mask_mode=1, causal_offset=297) <= 1.0
+    # one output ulp off somewhere breaks it
+    bad = ot.clone().float()
+    bad.view(-1)[5] = bad.view(-1)[5] * (1 + 2.0 ** -6)
+    assert attn_worst(bad.to(dtype), q, k, v, mask_mode=1, causal_offset=297) > 1.0

@@ -1,11 +1,12 @@
 """GPU parity and invariance tests of the batch-invariant attention (libbi.so bi_sdpa).
 
-Parity bar against the host oracle (the reference's per-key fold; the CUDA-core route
-runs that fold with the oracle's lane split, the tensor-core route -- 16-bit, D = 64 /
-128, GQA groups of 4k heads -- folds each partial's keys a stage of 4 at a time with
-tensor-core products; C-library expf in place of CUDA's): max |gpu - oracle| /
-max |oracle| <= 2e-6 for float32 and <= 1 ulp of the output type (relative to that
-scale) for float16 / bfloat16.
+Parity bar against the host oracle (the reference's per-key fold), elementwise
+(conftest.attn_worst): every output element within half an output ulp of the oracle's
+unrounded fp32 result (2 fp32 ulps for float32) plus tau * sum_i p_i |v_ij| / sum_i p_i,
+tau = 2^-20 on the CUDA-core route (the oracle's fold, lane split and order; C-library
+expf in place of CUDA's) and 2^-16 on the tensor-core route (16-bit, D = 64 / 128, GQA
+groups of 4k heads: score = scale * (q . k), a partial's keys folded 4 at a time,
+weights entering P.V as e_hi + e_lo).
 Accuracy against float64 follows the reference (tests/test_invariance.py:408-432):
 float32 < 2e-6, bfloat16 < 3e-2.  Invariance bar: 0 differing bits.
 """
@@ -16,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import batch_with, bits, randn, to_np
+from conftest import attn_worst, batch_with, bits, randn, to_np
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -82,8 +83,14 @@ def test_parity_against_oracle(bi, dtype, maskkind):
             g = torch.Generator().manual_seed(45)
             mask = (torch.rand(2, 1, qL, N, generator=g) > 0.1).cuda()
         y = bi.scaled_dot_product_attention(q, k, v, mask=mask)
-        want = _oracle(q, k, v, mask)
-        assert _close(y, want, dtype), (dtype, maskkind, H, Hkv, qL, N, D)
+        if mask == "causal":
+            worst = attn_worst(y, q, k, v, mask_mode=1, causal_offset=N - qL)
+        elif mask is not None:
+            worst = attn_worst(y, q, k, v, mask_mode=2, mask=torch.from_numpy(
+                np.asarray(_np_mask(mask, dtype), dtype=np.float32)).to(dtype))
+        else:
+            worst = attn_worst(y, q, k, v)
+        assert worst <= 1.0, (dtype, maskkind, H, Hkv, qL, N, D, worst)
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -94,7 +101,7 @@ def test_sinks_parity_and_effect(bi, dtype):
     v = randn((1, Hkv, N, D), dtype, 47, "cuda")
     sinks = randn((H,), dtype, 48, "cuda")
     y = bi.scaled_dot_product_attention(q, k, v, sinks=sinks)
-    assert _close(y, _oracle(q, k, v, sinks=sinks), dtype)
+    assert attn_worst(y, q, k, v, sinks=sinks) <= 1.0
 
 
 def test_accuracy_against_float64(bi):
