@@ -54,13 +54,9 @@ static __device__ __align__(256) uint32_t g_static_flag_block[BI_PEER_FLAG_BYTES
 namespace tc {
 
 constexpr int BM = kTcBM;    // rows per CTA (the pair covers 2*BM)
-constexpr int BN = kTcBN;    // columns per pair tile
-constexpr int BN_CTA = BN / 2;  // B columns each CTA loads
 constexpr int BK = kTcBK;    // 64 x 2 bytes = one 128-byte swizzle row
 constexpr int UMMA_K = 16;
-constexpr int B_STAGE_BYTES = BN_CTA * BK * 2;  // 16 KiB
 constexpr int ACC_BUFS = 2;
-constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512: the whole tensor memory of the SM
 constexpr int NUM_THREADS = 192;
 constexpr int EPI_WARPS = 4;
 // Epilogue staging: each epilogue warp turns 32 rows x 128 columns of finished outputs
@@ -71,25 +67,30 @@ constexpr int EPI_STAGE_BYTES = 32 * EPI_COLS * 2;  // per warp, 16-bit outputs
 // The shared-memory ring that feeds the UMMAs.  It decides how many rows of A each
 // stage holds and how many stages are in flight -- never the tile, the instruction or
 // the K order.
-//   WideRing  every CTA loads its 128 rows of A; 6 stages of 16 + 16 KiB.
-//   ThinRing  M <= 16: only rows 0-15 of the pair tile exist, so CTA 0 loads a
-//             16-row A box and CTA 1 none; the freed memory holds 10 stages, keeping
-//             160 KiB of W in flight per SM (decode is bound by streaming W).
-//             The UMMA still reads 128 rows per CTA: rows past the box hold whatever
-//             the shared memory held, which only reaches output rows >= 16 (>= M),
-//             and those are never stored.
+//   Wide ring  every CTA loads its 128 rows of A; 6 stages of 16 + 16 KiB.
+//   Thin ring  M <= 16: only rows 0-15 of the pair tile exist, so CTA 0 loads a
+//              16-row A box and CTA 1 none; the freed memory holds 10 stages, keeping
+//              160 KiB of W in flight per SM (decode is bound by streaming W).
+//              The UMMA still reads 128 rows per CTA: rows past the box hold whatever
+//              the shared memory held, which only reaches output rows >= 16 (>= M),
+//              and those are never stored.
 template <int A_ROWS_, int STAGES_>
 struct RingCfg {
   static constexpr int A_ROWS = A_ROWS_;
   static constexpr int STAGES = STAGES_;
+  static constexpr int BN = kTcBN;              // columns per pair tile
+  static constexpr int BN_CTA = BN / 2;         // B columns each CTA loads
+  static constexpr int TMEM_COLS = ACC_BUFS * BN;
   static constexpr bool THIN = A_ROWS_ < BM;
   static constexpr int A_STAGE_BYTES = A_ROWS * BK * 2;
+  static constexpr int B_STAGE_BYTES = BN_CTA * BK * 2;
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int NUM_BARRIERS = 2 * STAGES + 2 * ACC_BUFS + 1;
   static constexpr int SMEM_BYTES = 1024 /* alignment slack */ + STAGES * STAGE_BYTES +
                                     EPI_WARPS * EPI_STAGE_BYTES + NUM_BARRIERS * 8 + 16;
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory above the per-CTA limit");
-  static_assert(A_STAGE_BYTES % 1024 == 0, "A stages must keep 1 KiB swizzle alignment");
+  static_assert(A_STAGE_BYTES % 1024 == 0 && B_STAGE_BYTES % 1024 == 0,
+                "stages must keep 1 KiB swizzle alignment");
 };
 using WideRing = RingCfg<BM, 6>;
 using ThinRing = RingCfg<16, 10>;
@@ -142,6 +143,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const Params p) {
   constexpr int STAGES = R::STAGES;
+  constexpr int BN = R::BN;
+  constexpr int BN_CTA = R::BN_CTA;
+  constexpr int TMEM_COLS = R::TMEM_COLS;
+  constexpr int B_STAGE_BYTES = R::B_STAGE_BYTES;
   constexpr int A_STAGE_BYTES = R::A_STAGE_BYTES;
   constexpr int STAGE_BYTES = R::STAGE_BYTES;
   constexpr int NUM_BARRIERS = R::NUM_BARRIERS;
@@ -645,7 +650,7 @@ static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t str
   int st = make_map(&ma, g.a, g.M, g.K, g.lda, BK, R::A_ROWS, g.dtype);
   if (st) return st;
   if (B_NK) {
-    st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, BN_CTA, g.dtype);
+    st = make_map(&mb, g.b, g.N, g.K, g.ldb, BK, R::BN_CTA, g.dtype);
   } else {
     st = make_map(&mb, g.b, g.K, g.N, g.ldb, 64, BK, g.dtype);
   }
@@ -668,7 +673,7 @@ static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t str
   p.beta = g.beta;
   p.has_bias = g.bias != nullptr;
   p.tiles_m = static_cast<int>((g.M + 2 * BM - 1) / (2 * BM));
-  p.tiles_n = static_cast<int>((g.N + BN - 1) / BN);
+  p.tiles_n = static_cast<int>((g.N + R::BN - 1) / R::BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   if (gx != nullptr) {
     p.gx = *gx;

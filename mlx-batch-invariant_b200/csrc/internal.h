@@ -63,7 +63,8 @@ struct SdpaArgs {
   int64_t os[3];
 };
 
-// Fixed tile constants of the tensor-core route (bf16 / fp16).
+// Fixed tile constants of the tensor-core route (bf16 / fp16): 128 rows per CTA (a
+// 256 x 256 pair tile) and a 64-deep K block.
 constexpr int kTcBM = 128;
 constexpr int kTcBN = 256;
 constexpr int kTcBK = 64;

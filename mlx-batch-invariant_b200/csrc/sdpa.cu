@@ -990,12 +990,17 @@ static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "sdpa tc launch");
 }
 
-// Four query heads per CTA (a GQA group of 4k heads takes k CTAs); the kernel is
-// written for any of 1, 2 or 4 heads per CTA, which only decides which CTA computes
-// a row, but only 4 is routed here.
+// Query heads per CTA: 4 (every K/V fragment serves four MMA row groups), or 2 or 1
+// when four would leave the GPU short of CTAs (fewer than two per SM: decode on a
+// head shard, small batches).  Each (head, partial) is one MMA row whose value depends
+// only on its own q row and the key columns, whatever the other rows hold, so the
+// heads-per-CTA count decides which CTA computes a row, never the row's bits.
 template <typename T, int D>
 static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  return launch_gh<T, D, 4>(a, p, stream);
+  const int64_t want = 2LL * device_sm_count();
+  if (a.B * (a.H / 4) * a.qL >= want) return launch_gh<T, D, 4>(a, p, stream);
+  if (a.B * (a.H / 2) * a.qL >= want) return launch_gh<T, D, 2>(a, p, stream);
+  return launch_gh<T, D, 1>(a, p, stream);
 }
 
 }  // namespace tcr

@@ -12,9 +12,11 @@ import torch
 
 from . import _lib
 
-# The tensor-core tile used for float16 / bfloat16: fixed for every shape and every
-# M (cf. the reference's TILE, _gemm.py:27).  UMMA_* is the tcgen05 instruction.
-TILE = dict(BM=128, BN=256, BK=64, UMMA_M=128, UMMA_N=256, UMMA_K=16)
+# The tensor-core tile used for float16 / bfloat16, fixed for every shape and every M
+# (cf. the reference's TILE, _gemm.py:27): BM rows per CTA, a pair of CTAs
+# (CTA_GROUP = 2) on a 256 x BN tile, 64-deep K blocks, and the 2-SM tcgen05
+# instruction UMMA_M x UMMA_N x UMMA_K.
+TILE = dict(BM=128, BN=256, BK=64, UMMA_M=256, UMMA_N=256, UMMA_K=16, CTA_GROUP=2)
 # The CUDA-core tile (float32, and float16/bfloat16 when K % 8 != 0).
 SIMT_TILE = dict(BM=128, BN=128, BK=8)
 

@@ -51,7 +51,8 @@ def test_route_depends_on_k_n_dtype_layout_never_m():
     assert bi.tile_for(torch.bfloat16, 4095, 4096, True)["route"] == "simt"  # K % 8
     assert bi.tile_for(torch.bfloat16, 4096, 4095, False)["route"] == "simt"  # (K,N) row stride
     assert bi.tile_for(torch.bfloat16, 4096, 4095, True)["route"] == "tcgen05"
-    assert bi.TILE == dict(BM=128, BN=256, BK=64, UMMA_M=128, UMMA_N=256, UMMA_K=16)
+    assert bi.TILE == dict(BM=128, BN=256, BK=64, UMMA_M=256, UMMA_N=256, UMMA_K=16,
+                           CTA_GROUP=2)
 
 
 def test_gemm_argument_errors_are_status_codes():
