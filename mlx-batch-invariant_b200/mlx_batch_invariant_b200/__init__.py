@@ -20,6 +20,7 @@ import math
 import torch
 import torch.nn.functional as F
 
+from . import _ops  # noqa: F401  (registers mlx_bi::gemm and mlx_bi::sdpa)
 from ._attention import _mask_args, _sdpa, scaled_dot_product_attention
 from ._attention import MAX_HEAD_DIM
 from ._gemm import QUANT_BITS, SIMT_TILE, TILE, addmm, linear, matmul, quantized_linear, tile_for

@@ -73,6 +73,15 @@ def _aligned_heads(t, row_contiguous):
 
 
 def _sdpa(q, k, v, scale, mask_mode, causal_offset, m, mstrides, sinks):
+    """bi_sdpa on validated arguments; under torch.compile the opaque op mlx_bi::sdpa
+    (same implementation)."""
+    if torch.compiler.is_compiling():
+        return torch.ops.mlx_bi.sdpa(q, k, v, float(scale), int(mask_mode), int(causal_offset),
+                                     m, [int(x) for x in mstrides], sinks)
+    return _sdpa_eager(q, k, v, scale, mask_mode, causal_offset, m, mstrides, sinks)
+
+
+def _sdpa_eager(q, k, v, scale, mask_mode, causal_offset, m, mstrides, sinks):
     B, H, qL, D = q.shape
     _, Hkv, N, V = v.shape
     dev = q.device

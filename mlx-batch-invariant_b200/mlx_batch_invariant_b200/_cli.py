@@ -334,10 +334,10 @@ def main(argv=None):
         return verify(argv[1:])
     if argv and argv[0] == "decoder":
         return decoder(argv[1:])
-    print("usage: python -m mlx_batch_invariant_b200 verify [--quick] "
-          "[--dtype float32|float16|bfloat16] [--seed N]\n"
-          "       python -m mlx_batch_invariant_b200 decoder [--small] [--batch B] "
-          "[--prompt L] [--gen S] [--exchange fused|nccl] [--single-check]", file=sys.stderr)
+    print("usage: mlx-bi verify [--quick] [--dtype float32|float16|bfloat16] [--seed N]\n"
+          "       mlx-bi decoder [--small] [--batch B] [--prompt L] [--gen S] "
+          "[--exchange fused|nccl] [--single-check]\n"
+          "(or python -m mlx_batch_invariant_b200 ...)", file=sys.stderr)
     return 2
 
 

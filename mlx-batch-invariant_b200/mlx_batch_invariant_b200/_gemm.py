@@ -52,12 +52,23 @@ def _check_cuda(*ts):
 
 
 def _gemm(a, b, bias, transpose_b, alpha=1.0, beta=1.0, out=None):
-    """Validation follows mlx_batch_invariant/_gemm.py:_gemm (:185-222)."""
+    """Validation follows mlx_batch_invariant/_gemm.py:_gemm (:185-222).  Under
+    torch.compile the call is the opaque op mlx_bi::gemm (same implementation)."""
+    if out is None and torch.compiler.is_compiling():
+        _validate(a, b, bias, transpose_b)
+        if bias is not None and bias.dtype != a.dtype:
+            bias = bias.to(a.dtype)
+        return torch.ops.mlx_bi.gemm(a, b, bias, bool(transpose_b), float(alpha), float(beta))
+    return _gemm_eager(a, b, bias, transpose_b, alpha, beta, out)
+
+
+def _validate(a, b, bias, transpose_b):
+    """The reference's argument checks (_gemm.py:187-207); returns (lead, M, K, N)."""
     if a.dtype != b.dtype:
         raise ValueError("a and b must share a dtype, got %s and %s" % (a.dtype, b.dtype))
     if a.ndim < 2 or b.ndim != 2:
         raise ValueError("expected a.ndim >= 2 and b.ndim == 2")
-    code = _lib.dtype_code(a.dtype)
+    _lib.dtype_code(a.dtype)
     lead, K = tuple(a.shape[:-1]), a.shape[-1]
     M = 1
     for d in lead:
@@ -65,12 +76,19 @@ def _gemm(a, b, bias, transpose_b, alpha=1.0, beta=1.0, out=None):
     kb, N = (b.shape[1], b.shape[0]) if transpose_b else (b.shape[0], b.shape[1])
     if kb != K:
         raise ValueError("inner dimensions do not match: %d vs %d" % (K, kb))
-    if bias is not None:
-        if tuple(bias.shape) != (N,):
-            raise ValueError("bias must have shape (%d,), got %s" % (N, tuple(bias.shape)))
-        if bias.dtype != a.dtype:
-            bias = bias.to(a.dtype)
-    dev = _check_cuda(a, b, bias)
+    if bias is not None and tuple(bias.shape) != (N,):
+        raise ValueError("bias must have shape (%d,), got %s" % (N, tuple(bias.shape)))
+    _check_cuda(a, b, bias)
+    return lead, M, K, N
+
+
+def _gemm_eager(a, b, bias, transpose_b, alpha=1.0, beta=1.0, out=None):
+    """The libbi.so call behind matmul / addmm / linear (and the mlx_bi::gemm op)."""
+    lead, M, K, N = _validate(a, b, bias, transpose_b)
+    code = _lib.dtype_code(a.dtype)
+    if bias is not None and bias.dtype != a.dtype:
+        bias = bias.to(a.dtype)
+    dev = a.device
 
     a2 = _aligned(a.reshape(M, K))
     b2 = _aligned(b)

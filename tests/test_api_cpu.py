@@ -255,3 +255,35 @@ def test_static_allgather_rejects_a_rank_outside_the_world():
     st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 16, stages, cols, 1, 8, 1,
                                     1.0, 1.0, _lib.BI_BF16, devices, 2, 2, 1, None)
     assert st == -1 and b"rank" in L.bi_last_error()
+
+
+def test_mlx_bi_console_entry_point_is_declared_and_callable():
+    """The reference installs `mlx-bi` (pyproject.toml [project.scripts]); so does this
+    build, pointing at the same verify / decoder front end."""
+    import importlib
+    import tomllib
+    path = os.path.join(ROOT, "mlx-batch-invariant_b200", "pyproject.toml")
+    with open(path, "rb") as f:
+        meta = tomllib.load(f)
+    target = meta["project"]["scripts"]["mlx-bi"]
+    mod, func = target.split(":")
+    main = getattr(importlib.import_module(mod), func)
+    assert main([]) == 2  # usage on no sub-command, as `mlx-bi` alone
+    assert "libbi.so" in meta["tool"]["setuptools"]["package-data"]["mlx_batch_invariant_b200"]
+
+
+def test_custom_ops_are_registered_with_shape_only_fakes():
+    """mlx_bi::gemm and mlx_bi::sdpa (the opaque ops torch.compile sees) give the output
+    shape and dtype on fake tensors, without touching a GPU."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        a = torch.empty(3, 5, 64, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(96, 64, dtype=torch.bfloat16, device="cuda")
+        y = torch.ops.mlx_bi.gemm(a, w, None, True, 1.0, 1.0)
+        assert y.shape == (3, 5, 96) and y.dtype == torch.bfloat16
+        wk = torch.empty(64, 40, dtype=torch.bfloat16, device="cuda")
+        assert torch.ops.mlx_bi.gemm(a, wk, None, False, 1.0, 1.0).shape == (3, 5, 40)
+        q = torch.empty(2, 8, 3, 64, dtype=torch.float16, device="cuda")
+        k = torch.empty(2, 2, 10, 64, dtype=torch.float16, device="cuda")
+        o = torch.ops.mlx_bi.sdpa(q, k, k, 0.125, 1, 7, None, [0, 0, 0], None)
+        assert o.shape == (2, 8, 3, 64) and o.dtype == torch.float16
