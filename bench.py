@@ -335,12 +335,16 @@ def run_ours(args):
             if dom_events is not None and i == DOMINANT:
                 dom_events[0].record()
             if world > 1:
-                y = fused[i].linear(xs[K], ws[i], out=ys[i])
+                # the copy of the peers' blocks runs on a side stream, under the next GEMM
+                y = fused[i].linear(xs[K], ws[i], out=ys[i], wait=False)
             else:
                 y = bi.linear(xs[K], ws[i])
             if dom_events is not None and i == DOMINANT:
                 dom_events[1].record()
             outs.append(y)
+        if world > 1:
+            for f in fused:
+                f.finish()
         return outs
 
     def nccl_step():
@@ -417,7 +421,10 @@ def run_ours(args):
             "nvlink_bytes_out": link_bytes, "link_gbs": LINK_GBS,
             "link_peak_source": "measured peer copy, GB/s per direction per GPU",
             "target_us": target * 1e6, "achieved_us": dom_ms * 1e3,
-            "frac": target / (dom_ms / 1e3)}
+            "frac": target / (dom_ms / 1e3),
+            "scope": "entry barrier + GEMM with peer stores and exit barrier (the local "
+                     "unpack of the received blocks runs on a side stream under the next "
+                     "GEMM)"}
 
     # stock cuBLAS at the same shapes (the cost-of-invariance context)
     for _ in range(2):
@@ -435,18 +442,30 @@ def run_ours(args):
     cublas_tflops = local_flops * max(3, args.steps // 2) / (c0.elapsed_time(c1) / 1e3) / 1e12
 
     # ---- e2e: public API with host buffers
-    hx = {K: torch.empty((M, K), dtype=torch.bfloat16, pin_memory=True).copy_(xs[K].cpu())
-          for K in xs}
-    hy = [torch.empty((M, N), dtype=torch.bfloat16, pin_memory=True) for _, N in SHAPES]
-    h2d = sum(t.numel() * t.element_size() for t in hx.values())
-    d2h = sum(t.numel() * t.element_size() for t in hy)
+    # The job's inputs start in pinned host memory and its results end there.  One GPU:
+    # the whole x in and every output back.  N GPUs: each rank copies in its 1/N of x's
+    # rows, NCCL all-gathers x over NVLink, and copies back only its own column block
+    # of each output (the union over ranks is the whole result).  Copies run on their
+    # own streams and overlap the GEMMs: step it copies its inputs into device buffer
+    # it % 2 while the GEMMs of step it - 1 run, and each output block starts back to
+    # the host as soon as its GEMM is done.  Every byte is copied every step inside the
+    # timed region.
+    bounds_m = parallel.shard_bounds(M, world, align=1)
+    r0, r1 = bounds_m[rank]
+    hx = {K: torch.empty((r1 - r0, K), dtype=torch.bfloat16, pin_memory=True).copy_(
+        xs[K][r0:r1].cpu()) for K in xs}
+    col = [parallel.shard_bounds(N, world)[rank] for _, N in SHAPES]
+    hy = [torch.empty((M, c1 - c0), dtype=torch.bfloat16, pin_memory=True) for c0, c1 in col]
+    h2d_rank = sum(t.numel() * t.element_size() for t in hx.values())
+    d2h_rank = sum(t.numel() * t.element_size() for t in hy)
+    h2d = h2d_rank * world if world > 1 else h2d_rank
+    d2h = sum(M * N * 2 for _, N in SHAPES)
 
-    # One GPU: copies run on their own streams (the copy engines; PCIe is full duplex)
-    # and overlap the GEMMs: step it copies its inputs into device buffer it % 2 while
-    # the GEMMs of step it - 1 run, and each output starts back to the host as soon as
-    # its GEMM is done.  Every byte is still copied every step inside the timed region.
     copy_in, copy_out = torch.cuda.Stream(), torch.cuda.Stream()
+    xgather = torch.cuda.Stream() if world > 1 else None
     dx_bufs = [{K: torch.empty_like(xs[K]) for K in xs} for _ in range(2)]
+    dy_bufs = [[torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _, N in SHAPES]
+               for _ in range(2)] if world > 1 else None
     freed = [torch.cuda.Event() for _ in range(2)]  # last GEMM reading dx_bufs[b] done
     drained = [[torch.cuda.Event() for _ in SHAPES] for _ in range(2)]  # D2H of output b, i
     for b in range(2):
@@ -454,37 +473,44 @@ def run_ours(args):
         for e in drained[b]:
             e.record(main)
 
-    def e2e_step_serial():
-        # N > 1: copies in stream order with the fused calls (the layout measured across
-        # 2, 4 and 8 GPUs); the overlapped form below is the single-GPU path.
-        dx = {K: hx[K].to(dev, non_blocking=True) for K in hx}
-        for i, (K, N) in enumerate(SHAPES):
-            y = fused[i].linear(dx[K], ws[i], out=ys[i])
-            hy[i].copy_(y, non_blocking=True)
-
     def e2e_step(it):
-        if world > 1:
-            return e2e_step_serial()
         b = it & 1
         dx = dx_bufs[b]
         ready = {}
         with torch.cuda.stream(copy_in):
             copy_in.wait_event(freed[b])
             for K in hx:
-                dx[K].copy_(hx[K], non_blocking=True)
+                dx[K][r0:r1].copy_(hx[K], non_blocking=True)
                 ready[K] = torch.cuda.Event()
                 ready[K].record(copy_in)
+        if world > 1:
+            with torch.cuda.stream(xgather):
+                for K in hx:
+                    xgather.wait_event(ready[K])
+                    dist.all_gather_into_tensor(dx[K], dx[K][r0:r1])
+                    ready[K] = torch.cuda.Event()
+                    ready[K].record(xgather)
         for i, (K, N) in enumerate(SHAPES):
             main.wait_event(ready[K])
-            y = bi.linear(dx[K], ws[i])
+            if world > 1:
+                main.wait_event(drained[b][i])
+                y = fused[i].linear(dx[K], ws[i], out=dy_bufs[b][i], wait=False)
+                c0, c1 = col[i]
+                y_own = y[:, c0:c1]
+            else:
+                y = bi.linear(dx[K], ws[i])
+                y_own = y
             done = torch.cuda.Event()
             done.record(main)
             with torch.cuda.stream(copy_out):
                 copy_out.wait_event(done)
-                hy[i].copy_(y, non_blocking=True)
+                hy[i].copy_(y_own, non_blocking=True)
                 y.record_stream(copy_out)
                 drained[b][i].record(copy_out)
         freed[b].record(main)
+        if world > 1:
+            for f in fused:
+                f.finish()
 
     e2e_steps = max(3, min(args.steps, 10))
     for it in range(2):
@@ -498,6 +524,8 @@ def run_ours(args):
         e2e_step(it)
     main.wait_stream(copy_out)
     main.wait_stream(copy_in)
+    if xgather is not None:
+        main.wait_stream(xgather)
     f1.record(main)
     _barrier_sync(world)
     e2e_ms = _max_over_ranks(f0.elapsed_time(f1), world)
@@ -516,14 +544,20 @@ def run_ours(args):
                                "(8192,10240),(8192,8192),(8192,57344),(28672,8192), bf16",
                    "M": M, "shapes_KN": SHAPES,
                    "parallelism": ("column-parallel N over %d GPUs, all-gather fused into the "
-                                   "GEMM epilogue (NVLink peer stores of dense shard blocks, "
-                                   "local unpack)" % world) if world > 1
+                                   "GEMM epilogue (NVLink peer stores of dense shard blocks; "
+                                   "the local unpack on a side stream under the next GEMM)"
+                                   % world) if world > 1
                    else "single GPU",
                    "l2": "inputs larger than L2 (1.7 GB of weights), no flush"},
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "copies": ("pinned host buffers; H2D and D2H on their own streams, "
                            "overlapping the GEMMs (device inputs double-buffered)")
-                if world == 1 else "pinned host buffers; copies in stream order",
+                if world == 1 else
+                ("pinned host buffers on every rank: each copies in its 1/%d of x's rows "
+                 "(NCCL all-gather of x over NVLink) and copies back its own column block "
+                 "of every output; copies on their own streams overlapping the fused "
+                 "GEMMs; bytes are the whole job's (per rank: %d in, %d out)"
+                 % (world, h2d_rank, d2h_rank)),
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,

@@ -187,6 +187,31 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
                       void* stream);
 
 /*
+ * bi_gemm_allgather in two halves, so the local copy of the received blocks can run
+ * on another stream, under the next call's GEMM (no reference counterpart).
+ *
+ * bi_gemm_allgather_deferred takes bi_gemm_allgather's arguments and enqueues the
+ * entry barrier and the GEMM with its peer stores and exit barrier: on return (stream
+ * order) `out` holds this rank's own columns and every peer's block has landed in
+ * this rank's staging area.  bi_gather_unpack then copies those blocks into the other
+ * columns of `out` -- on `stream` after the GEMM (order it with an event when it is
+ * another stream).  Until that copy has run, this rank must make no further call on
+ * the same staging area (its entry barrier would let the peers overwrite it).
+ */
+int bi_gemm_allgather_deferred(const void* a, int64_t lda, const void* b, int64_t ldb,
+                               const void* bias, void* out, int64_t ldo,
+                               void* const* stages, const int64_t* cols,
+                               int64_t M, int64_t K, int b_is_nk,
+                               float alpha, float beta, int dtype,
+                               void* const* flags, int rank, int world, uint32_t epoch,
+                               void* stream);
+/* Copies rank s's dense (M, cols[s+1] - cols[s]) block, stored at element offset
+ * M * cols[s] of stages[rank], into columns [cols[s], cols[s+1]) of `out` (row stride
+ * ldo) for every s != rank.  Only stages[rank] is read. */
+int bi_gather_unpack(void* out, int64_t ldo, void* const* stages, const int64_t* cols,
+                     int64_t M, int rank, int world, int dtype, void* stream);
+
+/*
  * bi_gemm_allgather for callers that may not allocate device memory.  No counterpart
  * in the reference (which is single-device).
  *

@@ -322,10 +322,11 @@ int bi_peer_barrier(void* const* flags, int rank, int world, uint32_t epoch, voi
   return launch_peer_barrier(x, static_cast<cudaStream_t>(stream));
 }
 
-int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
-                      void* out, int64_t ldo, void* const* stages, const int64_t* cols,
-                      int64_t M, int64_t K, int b_is_nk, float alpha, float beta, int dtype,
-                      void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
+static int gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb,
+                          const void* bias, void* out, int64_t ldo, void* const* stages,
+                          const int64_t* cols, int64_t M, int64_t K, int b_is_nk, float alpha,
+                          float beta, int dtype, void* const* flags, int rank, int world,
+                          uint32_t epoch, void* stream, bool unpack) {
   g_msg[0] = '\0';
   if (dtype != BI_F16 && dtype != BI_BF16) {
     return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather takes fp16 or bf16");
@@ -368,7 +369,60 @@ int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, co
   void* out_shard = out != nullptr ? static_cast<uint16_t*>(out) + x.cols[rank] : nullptr;
   GemmArgs g{a, lda, b, ldb, bias, out_shard, ldo, M, n_local, K, b_is_nk ? 1 : 0,
              alpha, beta, dtype};
-  return launch_gemm_tc_allgather(g, x, out, s);
+  return launch_gemm_tc_allgather(g, x, out, s, unpack);
+}
+
+int bi_gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
+                      void* out, int64_t ldo, void* const* stages, const int64_t* cols,
+                      int64_t M, int64_t K, int b_is_nk, float alpha, float beta, int dtype,
+                      void* const* flags, int rank, int world, uint32_t epoch, void* stream) {
+  return gemm_allgather(a, lda, b, ldb, bias, out, ldo, stages, cols, M, K, b_is_nk, alpha, beta,
+                        dtype, flags, rank, world, epoch, stream, true);
+}
+
+int bi_gemm_allgather_deferred(const void* a, int64_t lda, const void* b, int64_t ldb,
+                               const void* bias, void* out, int64_t ldo, void* const* stages,
+                               const int64_t* cols, int64_t M, int64_t K, int b_is_nk,
+                               float alpha, float beta, int dtype, void* const* flags, int rank,
+                               int world, uint32_t epoch, void* stream) {
+  return gemm_allgather(a, lda, b, ldb, bias, out, ldo, stages, cols, M, K, b_is_nk, alpha, beta,
+                        dtype, flags, rank, world, epoch, stream, false);
+}
+
+int bi_gather_unpack(void* out, int64_t ldo, void* const* stages, const int64_t* cols, int64_t M,
+                     int rank, int world, int dtype, void* stream) {
+  g_msg[0] = '\0';
+  if (dtype != BI_F16 && dtype != BI_BF16) {
+    return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather takes fp16 or bf16");
+  }
+  if (M < 0) return set_error(BI_ERR_INVALID, "negative size");
+  if (stages == nullptr || cols == nullptr) {
+    return set_error(BI_ERR_INVALID, "stages and cols must not be null");
+  }
+  if (world < 1 || world > BI_MAX_PEERS || rank < 0 || rank >= world) {
+    return set_error(BI_ERR_INVALID, "rank %d / world %d outside [0, %d)", rank, world,
+                     BI_MAX_PEERS);
+  }
+  GatherArgs x{};
+  if (cols[0] != 0) return set_error(BI_ERR_INVALID, "cols[0] must be 0");
+  for (int r = 0; r <= world; ++r) {
+    if (r > 0 && cols[r] < cols[r - 1]) return set_error(BI_ERR_INVALID, "cols must be nondecreasing");
+    if (cols[r] % 8 != 0) return set_error(BI_ERR_MISALIGNED, "column bounds must be multiples of 8");
+    x.cols[r] = cols[r];
+  }
+  if (stages[rank] == nullptr) return set_error(BI_ERR_INVALID, "this rank's staging area is null");
+  x.stages[rank] = stages[rank];
+  x.rank = rank;
+  x.world = world;
+  if (ldo % 8 != 0 || ldo < x.cols[world]) {
+    return set_error(BI_ERR_MISALIGNED, "ldo must be a multiple of 8 and at least cols[world]");
+  }
+  if (M > 0 && x.cols[world] > 0 && (out == nullptr || !aligned16(out) || !aligned16(stages[rank]))) {
+    return set_error(BI_ERR_MISALIGNED, "out and the staging area must be 16-byte aligned");
+  }
+  int st = check_device();
+  if (st) return st;
+  return launch_gather_unpack(x, out, ldo, M, static_cast<cudaStream_t>(stream));
 }
 
 int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,

@@ -717,7 +717,7 @@ int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream) {
 }
 
 int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, void* out_base,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, bool unpack) {
   if (g.M > INT32_MAX || g.N > INT32_MAX || g.K > INT32_MAX) {
     return set_error(BI_ERR_UNSUPPORTED, "dimensions above 2^31 are not supported");
   }
@@ -730,18 +730,24 @@ int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, void* out_b
   } else {
     st = tc::dispatch<true>(g, &x, stream);
   }
-  if (st || g.M == 0 || x.world == 1) return st;
+  if (st || !unpack) return st;
   // Every peer has posted its exit epoch once the kernel above ends: unpack their blocks.
+  return launch_gather_unpack(x, out_base, g.ldo, g.M, stream);
+}
+
+int launch_gather_unpack(const GatherArgs& x, void* out_base, int64_t ldo, int64_t M,
+                         cudaStream_t stream) {
+  if (M == 0 || x.world == 1) return BI_OK;
   int64_t most = 0;
   for (int r = 0; r < x.world; ++r) {
-    if (r != x.rank) most = std::max(most, g.M * ((x.cols[r + 1] - x.cols[r]) >> 3));
+    if (r != x.rank) most = std::max(most, M * ((x.cols[r + 1] - x.cols[r]) >> 3));
   }
   if (most == 0) return BI_OK;
   const int64_t per_cta = static_cast<int64_t>(tc::UNPACK_THREADS) * tc::UNPACK_UNROLL;
   const int64_t want = (most + per_cta - 1) / per_cta;
   const int ctas = static_cast<int>(std::min<int64_t>(want, 4 * device_sm_count()));
   tc::gather_unpack_kernel<<<dim3(ctas, x.world - 1), tc::UNPACK_THREADS, 0, stream>>>(
-      x, static_cast<uint16_t*>(out_base), g.ldo, g.M);
+      x, static_cast<uint16_t*>(out_base), ldo, M);
   return cuda_status(cudaGetLastError(), "gather unpack launch");
 }
 

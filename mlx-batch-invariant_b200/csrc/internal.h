@@ -98,8 +98,12 @@ int launch_swiglu(const void* gu, void* out, int64_t M, int64_t I, int dtype,
 
 int launch_gemm_tc(const GemmArgs& g, cudaStream_t stream);
 // g.out points at column cols[rank] of the output whose first column is out_base.
+// unpack = false leaves the peers' blocks in this rank's staging area (launch
+// launch_gather_unpack later, possibly on another stream).
 int launch_gemm_tc_allgather(const GemmArgs& g, const GatherArgs& x, void* out_base,
-                             cudaStream_t stream);
+                             cudaStream_t stream, bool unpack);
+int launch_gather_unpack(const GatherArgs& x, void* out_base, int64_t ldo, int64_t M,
+                         cudaStream_t stream);
 int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream);
 int static_flag_block(int device, void** out);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);

@@ -94,6 +94,12 @@ def _distributed_checks(dtypes, gen_seed, dev):
                         xr = x[:rows] if rows <= 33 else torch.cat([x, x[:31]])
                         y = fused.linear(xr, ws, bs)
                         ok = ok and torch.equal(_bits(y), _bits(linear(xr, w, b)))
+                    # the unpack deferred to a side stream, two calls in flight
+                    xs2 = [x, torch.cat([x, x[:31]])]
+                    ys2 = [fused.linear(xr, ws, bs, wait=False) for xr in xs2]
+                    fused.finish()
+                    for xr, y in zip(xs2, ys2):
+                        ok = ok and torch.equal(_bits(y), _bits(linear(xr, w, b)))
                 finally:
                     fused.close()
                 fails += not ok

@@ -76,6 +76,11 @@ def _bind(lib):
     tail = [ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _vp]
     lib.bi_gemm_allgather.restype = ctypes.c_int
     lib.bi_gemm_allgather.argtypes = gather + [ctypes.POINTER(_vp)] + tail
+    lib.bi_gemm_allgather_deferred.restype = ctypes.c_int
+    lib.bi_gemm_allgather_deferred.argtypes = gather + [ctypes.POINTER(_vp)] + tail
+    lib.bi_gather_unpack.restype = ctypes.c_int
+    lib.bi_gather_unpack.argtypes = [_vp, _i64, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]
     lib.bi_gemm_allgather_static.restype = ctypes.c_int
     lib.bi_gemm_allgather_static.argtypes = gather + [ctypes.POINTER(ctypes.c_int)] + tail
     lib.bi_rope_kv.restype = ctypes.c_int

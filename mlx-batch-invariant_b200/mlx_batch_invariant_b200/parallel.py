@@ -202,14 +202,22 @@ class FusedColumnParallel:
             raise
         self._stages = (ctypes.c_void_p * self.world)(*self._ptrs)
         self._flags = (ctypes.c_void_p * self.world)(*[p + self._stage_bytes for p in self._ptrs])
+        self._side = None      # stream of the deferred unpacks (linear(..., wait=False))
+        self._pending = None   # event: the last deferred unpack has run
 
     @property
     def shard_rows(self):
         return self.col1 - self.col0
 
-    def linear(self, x, w_shard, bias_shard=None, out=None):
+    def linear(self, x, w_shard, bias_shard=None, out=None, wait=True):
         """y = x @ w.T (+ bias) on all ranks; w_shard is this rank's (shard, K) rows.
-        `out`, if given, is a contiguous (..., n_total) tensor on x's device."""
+        `out`, if given, is a contiguous (..., n_total) tensor on x's device.
+
+        wait=False leaves the copy of the peers' blocks into `out` to a side stream,
+        where it overlaps whatever the current stream runs next (the next call's GEMM):
+        on return this rank's own columns are ready in stream order, the others only
+        after ``finish()`` -- call it before anything on the current stream reads them.
+        """
         if x.dtype != self.dtype or w_shard.dtype != self.dtype:
             raise ValueError("x and w must be %s" % self.dtype)
         if w_shard.shape[0] != self.shard_rows:
@@ -233,19 +241,47 @@ class FusedColumnParallel:
         w2 = _aligned(w_shard) if w_shard.shape[0] else w_shard
         b2 = bias_shard.to(self.dtype).contiguous() if bias_shard is not None else None
         dev = x.device
-        with torch.cuda.device(dev):
-            st = _lib.lib().bi_gemm_allgather(
-                x2.data_ptr(), K, w2.data_ptr() if w2.numel() else None, K,
+        cur = torch.cuda.current_stream(dev)
+        if self._pending is not None:
+            # the previous deferred unpack reads the staging area this call's entry
+            # barrier hands back to the peers
+            cur.wait_event(self._pending)
+            self._pending = None
+        L = _lib.lib()
+        args = (x2.data_ptr(), K, w2.data_ptr() if w2.numel() else None, K,
                 b2.data_ptr() if b2 is not None else None, out.data_ptr(), self.n_total,
                 self._stages, self._cols, M, K, 1, 1.0, 1.0, _lib.dtype_code(self.dtype),
-                self._flags, self.rank, self.world, 0, _lib.stream_handle(dev))
-        _lib.check(st, "bi_gemm_allgather")
+                self._flags, self.rank, self.world, 0)
+        with torch.cuda.device(dev):
+            if wait:
+                _lib.check(L.bi_gemm_allgather(*args, cur.cuda_stream), "bi_gemm_allgather")
+                return out
+            _lib.check(L.bi_gemm_allgather_deferred(*args, cur.cuda_stream),
+                       "bi_gemm_allgather_deferred")
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=dev)
+            done = torch.cuda.Event()
+            done.record(cur)
+            self._side.wait_event(done)
+            _lib.check(L.bi_gather_unpack(out.data_ptr(), self.n_total, self._stages, self._cols,
+                                          M, self.rank, self.world, _lib.dtype_code(self.dtype),
+                                          self._side.cuda_stream), "bi_gather_unpack")
+            out.record_stream(self._side)
+            self._pending = torch.cuda.Event()
+            self._pending.record(self._side)
         return out
+
+    def finish(self):
+        """Orders the current stream after the last deferred unpack (linear(...,
+        wait=False)): from here on its output holds every rank's columns."""
+        if self._pending is not None:
+            torch.cuda.current_stream().wait_event(self._pending)
 
     def close(self):
         """Unmaps the peers' buffers and frees this one (collective)."""
         if self._local is None:
             return
+        self.finish()
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         L = _lib.lib()
