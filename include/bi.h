@@ -219,30 +219,38 @@ int bi_gather_unpack(void* out, int64_t ldo, void* const* stages, const int64_t*
  * cudaMalloc.  Some callers cannot do that: a serving process whose device memory is
  * all handed out up front by its own allocator (weights, KV cache, activation arena)
  * and which must not have a library take memory behind that allocator's back, or a
- * host program that only ever passes buffers it owns.  This entry point takes no
- * flag blocks: each rank's block is its device's copy of a 256-byte file-scope
- * device array inside libbi.so (BI_PEER_FLAG_BYTES per device, held by every GPU that
- * loads the library until the process exits).  Everything else is as in
- * bi_gemm_allgather, and it calls no cudaMalloc, cudaFree or other allocating routine.
+ * host program that only ever passes buffers it owns.  This entry point allocates
+ * nothing and calls no cudaMalloc, cudaFree or other allocating routine.  The fused
+ * GEMM's own scratch -- its CTA-completion counter and the call count -- lives in a
+ * 256-byte file-scope device array inside libbi.so (one copy per GPU that loads the
+ * library, held until the process exits, touched only by kernels on that GPU); the
+ * flags the ranks post to one another sit at the head of the exchange areas the
+ * caller passes, which the peers must reach anyway.
  *
+ *   stages[r]   rank r's exchange area, mapped here: BI_PEER_FLAG_BYTES bytes of
+ *               flags (zero them once, before the first call; later calls use what
+ *               earlier ones left), then the staging area of bi_gemm_allgather
+ *               (M * cols[world] elements) -- at least BI_PEER_FLAG_BYTES + 2 * M *
+ *               cols[world] bytes, 16-byte aligned.
  *   devices[r]  the CUDA device ordinal rank r runs on, all in THIS process (one
  *               process drives every rank), one rank per device: a repeated ordinal
  *               is rejected (BI_ERR_INVALID), and so is a call whose devices[rank]
  *               is not the current device.  The call enables peer access from the
  *               current device to every other rank's device (already enabled counts
  *               as success) and returns BI_ERR_UNSUPPORTED where the hardware has
- *               none; stages[r] must be addressable from each of these devices.
+ *               none.
  *   world       at most BI_MAX_PEERS; larger values are rejected (BI_ERR_INVALID)
- *               because the static block holds flags for BI_MAX_PEERS ranks.
+ *               because the flag block holds flags for BI_MAX_PEERS ranks.
+ * Everything else is as in bi_gemm_allgather.
  *
- * The first call that names a device looks up its copy of the array with that
- * device current (cudaGetSymbolAddress) and caches the address; make that first call
- * before any stream capture.  All calls on a device share its block, which keeps the
- * last call's contents: each call clears the block's CTA counter on `stream` before
- * use, and `epoch` must exceed the epoch of every earlier call on the same devices (or
- * be 0 on every call: the block then counts the calls itself).
- * Calls whose work overlaps on the GPU (different streams, or different rank groups
- * sharing a device) race on the block.
+ * The first call on a device looks up its copy of the array with that device current
+ * (cudaGetSymbolAddress) and caches the address; make that first call before any
+ * stream capture.  All calls on a device share the array, which keeps the last call's
+ * contents: each call clears the CTA counter on `stream` before use, and `epoch` must
+ * exceed the epoch of every earlier call on the same exchange areas (or be 0 on every
+ * call on the device: the array then counts the calls itself).  Calls whose work
+ * overlaps on the GPU (different streams, or different rank groups sharing a device)
+ * race on the array.
  */
 int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t ldb,
                              const void* bias, void* out, int64_t ldo,

@@ -294,6 +294,7 @@ static int gather_args(void* const* stages, void* const* flags, const int64_t* c
     x->flags[r] = static_cast<uint32_t*>(flags[r]);
     x->stages[r] = stages != nullptr ? stages[r] : nullptr;
   }
+  x->local = x->flags[rank];
   if (cols != nullptr) {
     if (cols[0] != 0) return set_error(BI_ERR_INVALID, "cols[0] must be 0");
     for (int r = 0; r <= world; ++r) {
@@ -326,7 +327,8 @@ static int gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb
                           const void* bias, void* out, int64_t ldo, void* const* stages,
                           const int64_t* cols, int64_t M, int64_t K, int b_is_nk, float alpha,
                           float beta, int dtype, void* const* flags, int rank, int world,
-                          uint32_t epoch, void* stream, bool unpack) {
+                          uint32_t epoch, void* stream, bool unpack,
+                          uint32_t* local = nullptr) {
   g_msg[0] = '\0';
   if (dtype != BI_F16 && dtype != BI_BF16) {
     return set_error(BI_ERR_UNSUPPORTED, "the fused all-gather takes fp16 or bf16");
@@ -338,6 +340,7 @@ static int gemm_allgather(const void* a, int64_t lda, const void* b, int64_t ldb
   GatherArgs x;
   int st = gather_args(stages, flags, cols, rank, world, epoch, &x);
   if (st) return st;
+  if (local != nullptr) x.local = local;
   const int64_t n_total = x.cols[world];
   const int64_t n_local = x.cols[rank + 1] - x.cols[rank];
   if (ldo % 8 != 0 || ldo < n_total) {
@@ -433,27 +436,35 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
   g_msg[0] = '\0';
   if (world < 1 || world > BI_MAX_PEERS) {
     return set_error(BI_ERR_INVALID,
-                     "bi_gemm_allgather_static: world %d outside [1, %d] -- the static flag "
-                     "block holds flags for at most %d ranks",
+                     "bi_gemm_allgather_static: world %d outside [1, %d] -- the exchange "
+                     "flags hold at most %d ranks",
                      world, BI_MAX_PEERS, BI_MAX_PEERS);
   }
   if (devices == nullptr) return set_error(BI_ERR_INVALID, "devices is null");
   if (rank < 0 || rank >= world) return set_error(BI_ERR_INVALID, "rank outside [0, world)");
-  // One rank per device: two ranks on one device would share its block (the CTA counter
-  // and the flags), and one rank's counter reset could land in the other's call.
+  if (stages == nullptr) return set_error(BI_ERR_INVALID, "stages is null");
+  // One rank per device: two ranks on one device would share its counters (the CTA
+  // counter and the call count), and one rank's counter reset could land in the
+  // other's call.
   for (int r = 0; r < world; ++r) {
     for (int r2 = r + 1; r2 < world; ++r2) {
       if (devices[r] == devices[r2]) {
         return set_error(BI_ERR_INVALID,
                          "bi_gemm_allgather_static: ranks %d and %d are both on device %d; "
-                         "the static flag block holds one rank per device",
+                         "the static counters hold one rank per device",
                          r, r2, devices[r]);
       }
     }
   }
+  for (int r = 0; r < world; ++r) {
+    if (stages[r] == nullptr || !aligned16(stages[r])) {
+      return set_error(BI_ERR_MISALIGNED, "exchange area of rank %d is null or not 16-byte "
+                       "aligned", r);
+    }
+  }
   int st = check_device();
   if (st) return st;
-  // The local GEMM counts its CTAs in the block of the device it runs on.
+  // The local GEMM counts its CTAs in the array of the device it runs on.
   const int cur = current_device();
   if (devices[rank] != cur) {
     return set_error(BI_ERR_INVALID,
@@ -461,26 +472,31 @@ int bi_gemm_allgather_static(const void* a, int64_t lda, const void* b, int64_t 
                      "call each rank with its own device current",
                      rank, devices[rank], cur);
   }
-  // The kernels store into every other rank's block and staging area: this device must
-  // reach each of those devices' memory.
+  // The kernels store into every other rank's exchange area: this device must reach
+  // each of those devices' memory.
   for (int r = 0; r < world; ++r) {
     if (r == rank) continue;
     st = ensure_peer_access(cur, devices[r]);
     if (st) return st;
   }
-  // Each rank's flag block is its device's copy of the library's static array.
+  void* local = nullptr;
+  st = static_flag_block(cur, &local);
+  if (st) return st;
+  // Each exchange area starts with the rank's flag block; its staging area follows.
   void* flags[BI_MAX_PEERS] = {};
+  void* data[BI_MAX_PEERS] = {};
   for (int r = 0; r < world; ++r) {
-    st = static_flag_block(devices[r], &flags[r]);
-    if (st) return st;
+    flags[r] = stages[r];
+    data[r] = static_cast<uint8_t*>(stages[r]) + BI_PEER_FLAG_BYTES;
   }
-  // The block keeps the previous call's contents; the CTA counter must start at zero.
+  // The array keeps the previous call's contents; the CTA counter must start at zero.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(static_cast<uint32_t*>(flags[rank]) + kFlagCounter, 0,
+  cudaError_t e = cudaMemsetAsync(static_cast<uint32_t*>(local) + kFlagCounter, 0,
                                   sizeof(uint32_t), s);
   if (e != cudaSuccess) return cuda_status(e, "clearing the static CTA counter");
-  return bi_gemm_allgather(a, lda, b, ldb, bias, out, ldo, stages, cols, M, K, b_is_nk, alpha,
-                           beta, dtype, flags, rank, world, epoch, stream);
+  return gemm_allgather(a, lda, b, ldb, bias, out, ldo, data, cols, M, K, b_is_nk, alpha, beta,
+                        dtype, flags, rank, world, epoch, stream, true,
+                        static_cast<uint32_t*>(local));
 }
 
 int bi_rope_kv(const void* qkv, int64_t B, int64_t L, int64_t hq, int64_t hk, int64_t hd,

@@ -45,10 +45,10 @@
 
 namespace bi {
 
-// Scratch of bi_gemm_allgather_static: the epoch-flag block (exit and entry flags and
-// the CTA counter) kept in a file-scope device array instead of caller-allocated
-// memory.  Every device that loads this library holds its own 256-byte copy until the
-// process exits; all calls on a device share it.
+// Scratch of bi_gemm_allgather_static: the local GEMM's CTA-completion counter and the
+// call count, kept in a file-scope device array instead of caller-allocated memory.
+// Every device that loads this library holds its own 256-byte copy until the process
+// exits; all calls on a device share it, and only kernels on that device touch it.
 static __device__ __align__(256) uint32_t g_static_flag_block[BI_PEER_FLAG_BYTES / 4];
 
 namespace tc {
@@ -135,7 +135,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 // entry barrier stored in the local flag block.
 __device__ __forceinline__ uint32_t call_epoch(const GatherArgs& x) {
   return x.epoch != 0 ? x.epoch
-                      : *reinterpret_cast<volatile uint32_t*>(x.flags[x.rank] + kFlagEpoch);
+                      : *reinterpret_cast<volatile uint32_t*>(x.local + kFlagEpoch);
 }
 
 template <typename T, bool B_NK, bool GATHER, typename R>
@@ -480,7 +480,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
       // Every CTA's stores are fenced; the last CTA to count itself in publishes the
       // epoch to every rank and waits for every rank's.
-      uint32_t* counter = p.gx.flags[p.gx.rank] + kFlagCounter;
+      uint32_t* counter = p.gx.local + kFlagCounter;
       __threadfence_system();
       if (atomicAdd(counter, 1u) == gridDim.x - 1) {
         *counter = 0;  // the next call's CTAs start from zero (stream order)
@@ -553,7 +553,7 @@ __global__ void peer_barrier_kernel(const GatherArgs x, int slot) {
   uint32_t* own = x.flags[x.rank];
   uint32_t epoch = x.epoch;
   if (epoch == 0) {
-    epoch = *reinterpret_cast<volatile uint32_t*>(own + kFlagEpoch);
+    epoch = *reinterpret_cast<volatile uint32_t*>(x.local + kFlagEpoch);
     if (slot == kFlagEntry) epoch += 1;
   }
   __threadfence_system();
@@ -566,7 +566,7 @@ __global__ void peer_barrier_kernel(const GatherArgs x, int slot) {
                  ((slot == kFlagEntry ? kSitePeerEntry : kSitePeerExit) << 8) | kErrReasonTimeout);
   }
   __syncwarp();
-  if (x.epoch == 0 && slot == kFlagEntry && t == 0) own[kFlagEpoch] = epoch;
+  if (x.epoch == 0 && slot == kFlagEntry && t == 0) x.local[kFlagEpoch] = epoch;
 }
 
 // ---------------------------------------------------------------------------

@@ -31,14 +31,19 @@ struct GemmArgs {
 struct GatherArgs {
   void* stages[BI_MAX_PEERS];     // every rank's staging area, mapped here
   uint32_t* flags[BI_MAX_PEERS];  // every rank's flag block, mapped here
+  uint32_t* local;                // this rank's counters (its own device's memory only)
   int64_t cols[BI_MAX_PEERS + 1]; // column partition: rank s owns [cols[s], cols[s+1])
   int rank, world;
   uint32_t epoch;
 };
 
 // Flag block layout (32-bit words): [0, 8) exit flags posted by rank r, [8, 16) entry
-// flags posted by rank r, [16] CTA-completion counter of the local GEMM, [17] the
-// block's own call count (the epoch of calls made with epoch 0).
+// flags posted by rank r -- written by every rank -- and, in the block `local` points
+// at, [16] the CTA-completion counter of the local GEMM and [17] the call count (the
+// epoch of calls made with epoch 0) -- touched by this rank alone.  bi_gemm_allgather
+// keeps both halves in one block (local = flags[rank]); bi_gemm_allgather_static keeps
+// the counters in the library's own per-device array and the flags in the callers'
+// exchange areas, so no device touches another device's copy of that array.
 constexpr int kFlagExit = 0;
 constexpr int kFlagEntry = BI_MAX_PEERS;
 constexpr int kFlagCounter = 2 * BI_MAX_PEERS;

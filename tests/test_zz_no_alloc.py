@@ -1,7 +1,8 @@
 """bi_gemm_allgather_static: the fused column-parallel GEMM for callers that may not
 allocate device memory (a server whose allocator owns all of HBM, a host that only
-passes buffers it owns), whose epoch-flag block lives in a static device array inside
-libbi.so instead of memory from bi_peer_alloc.
+passes buffers it owns).  Its scratch (the CTA counter and the call count) lives in a
+static device array inside libbi.so instead of memory from bi_peer_alloc; the flags
+ranks post to one another sit at the head of the exchange areas the caller passes.
 
 Called through the C ABI on one GPU (world = 1), twice in a row, and checked against
 the existing entry point bi_gemm_allgather on the same inputs.  Both run the same
@@ -37,9 +38,12 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
     flags = (ctypes.c_void_p * 1)(flag_ptr.value)
     devices = (ctypes.c_int * 1)(dev)
     cols = (ctypes.c_int64 * 2)(0, N)
-    # one rank: no peer stores into the staging area, which must still be given
+    # one rank: no peer stores into the staging area, which must still be given; the
+    # static entry's exchange area is a zeroed flag block followed by that area
     stage = torch.empty(M * N, dtype=torch.bfloat16, device="cuda")
     stages = (ctypes.c_void_p * 1)(stage.data_ptr())
+    xarea = torch.zeros(_lib.PEER_FLAG_BYTES // 2 + M * N, dtype=torch.bfloat16, device="cuda")
+    xareas = (ctypes.c_void_p * 1)(xarea.data_ptr())
     try:
         for call in (1, 2):  # two calls in a row: the static block is reused
             x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
@@ -51,7 +55,7 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
                 x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), want.data_ptr(), N, stages, cols,
                 M, K, 1, 1.0, 1.0, _lib.BI_BF16, flags, 0, 1, call, stream), "bi_gemm_allgather")
             _lib.check(L.bi_gemm_allgather_static(
-                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), got.data_ptr(), N, stages, cols,
+                x.data_ptr(), K, w.data_ptr(), K, b.data_ptr(), got.data_ptr(), N, xareas, cols,
                 M, K, 1, 1.0, 1.0, _lib.BI_BF16, devices, 0, 1, call, stream),
                 "bi_gemm_allgather_static")
             torch.cuda.synchronize()
@@ -67,13 +71,14 @@ def test_static_scratch_allgather_matches_the_allocating_entry_point():
 def test_static_scratch_rejects_more_ranks_than_it_holds():
     from mlx_batch_invariant_b200 import _lib
     L = _lib.lib()
-    devices = (ctypes.c_int * 9)(*([torch.cuda.current_device()] * 9))
+    devices = (ctypes.c_int * 9)(*range(9))
     stages = (ctypes.c_void_p * 9)()
     cols = (ctypes.c_int64 * 10)(*range(0, 80, 8))
     st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 72, stages, cols, 1, 8, 1,
                                     1.0, 1.0, _lib.BI_BF16, devices, 0, 9, 1, None)
     assert st == -1
     assert b"at most 8 ranks" in L.bi_last_error()
+
 
 
 def test_static_scratch_rejects_a_rank_whose_device_is_not_current():
@@ -83,7 +88,8 @@ def test_static_scratch_rejects_a_rank_whose_device_is_not_current():
     L = _lib.lib()
     other = torch.cuda.current_device() + 1
     devices = (ctypes.c_int * 1)(other)
-    stages = (ctypes.c_void_p * 1)()
+    area = torch.zeros(256, dtype=torch.bfloat16, device="cuda")
+    stages = (ctypes.c_void_p * 1)(area.data_ptr())
     cols = (ctypes.c_int64 * 2)(0, 8)
     st = L.bi_gemm_allgather_static(None, 8, None, 8, None, None, 8, stages, cols, 1, 8, 1,
                                     1.0, 1.0, _lib.BI_BF16, devices, 0, 1, 1, None)
@@ -94,9 +100,9 @@ def test_static_scratch_rejects_a_rank_whose_device_is_not_current():
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_static_scratch_two_devices_in_one_process_match_one_gpu():
     """Two ranks driven by one process on devices 0 and 1: real peer stores into the
-    other device's staging area and static flag block.  The gathered output of both
-    ranks, on two calls in a row, equals bi_gemm of the full weight on one GPU, and
-    equals the allocating entry point's (flag blocks from bi_peer_alloc)."""
+    other device's staging area and flags.  The gathered output of both ranks, on two
+    calls in a row, equals bi_gemm of the full weight on one GPU, and equals the
+    allocating entry point's (flag blocks from bi_peer_alloc)."""
     from mlx_batch_invariant_b200 import _lib
     L = _lib.lib()
     M, K, N = 300, 1024, 1536
@@ -105,6 +111,10 @@ def test_static_scratch_two_devices_in_one_process_match_one_gpu():
     g = torch.Generator().manual_seed(77)
     stages = [torch.empty(M * N, dtype=torch.bfloat16, device="cuda:%d" % r) for r in range(2)]
     stage_ptrs = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in stages])
+    # the static entry's exchange areas: a zeroed flag block, then the staging area
+    xareas = [torch.zeros(_lib.PEER_FLAG_BYTES // 2 + M * N, dtype=torch.bfloat16,
+                          device="cuda:%d" % r) for r in range(2)]
+    xarea_ptrs = (ctypes.c_void_p * 2)(*[t.data_ptr() for t in xareas])
     flag_ptrs = []
     for r in range(2):
         with torch.cuda.device(r):
@@ -132,7 +142,7 @@ def test_static_scratch_two_devices_in_one_process_match_one_gpu():
                         if entry == "static":
                             st = L.bi_gemm_allgather_static(
                                 xs.data_ptr(), K, ws.data_ptr(), K, bs.data_ptr(), out.data_ptr(),
-                                N, stage_ptrs, cols, M, K, 1, 1.0, 1.0, _lib.BI_BF16, devices, r,
+                                N, xarea_ptrs, cols, M, K, 1, 1.0, 1.0, _lib.BI_BF16, devices, r,
                                 2, call, stream)
                         else:
                             st = L.bi_gemm_allgather(
