@@ -25,8 +25,9 @@ Also reported:
             the reference itself is Metal-only) on a bounded sample, rank 0, N = 1.
 
 --impl reference times that CPU implementation alone on the same metric (rank 0).
---profile gemm|sdpa runs 3 warm-up launches and 1 launch of one kernel at the bench's
-own dominant shape and prints nothing (the target of the committed ncu captures).
+--profile gemm|gemm-decode|sdpa runs 3 warm-up launches and 1 launch of one kernel (the
+bench's dominant GEMM, config 5's M = 1 GEMM on (28672, 8192), or the bench's decode
+attention) and prints nothing (the target of the committed ncu captures).
 --sweep prints config 5's table: bi.linear vs cuBLAS at M in 1..16384 on every shape.
 """
 
@@ -647,9 +648,10 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
-    if args.profile == "gemm":
-        K, N = SHAPES[DOMINANT]
-        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    if args.profile in ("gemm", "gemm-decode"):
+        # the bench's dominant GEMM, or config 5's decode case M = 1 on (28672, 8192)
+        (K, N), rows = (SHAPES[DOMINANT], M) if args.profile == "gemm" else (SHAPES[3], 1)
+        x = torch.randn((rows, K), generator=g, device=dev).to(torch.bfloat16)
         w = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
         for _ in range(4):
             bi.linear(x, w)
@@ -720,7 +722,7 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--profile", choices=["gemm", "sdpa"], default=None)
+    p.add_argument("--profile", choices=["gemm", "gemm-decode", "sdpa"], default=None)
     p.add_argument("--sweep", action="store_true",
                    help="config 5's M sweep on one GPU (a markdown table, no JSON line)")
     args = p.parse_args(argv)

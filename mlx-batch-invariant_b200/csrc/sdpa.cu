@@ -491,19 +491,24 @@ constexpr int R = 4;                 // keys per partial per stage
 constexpr int KEYS = PARTIALS * R;   // keys per stage
 constexpr int BOX_D = 64;            // columns per TMA box (128-byte rows)
 
-// Two CTAs per SM (128 registers, ~66 KB each): one 128-key stage of K and V per CTA
-// at D = 128 (two at D = 64), the other CTA's stages covering this one's latency.  The
-// region before the barriers holds the stage ring, and after the walk the combine's
-// partials (up to 4 heads x 32 partials x D floats, their m / l and denominators).
+// Stage ring of STAGES 128-key stages of K and V (the default: one at D = 128, two at
+// D = 64, with two CTAs per SM at 128 registers -- the other CTA's stages cover this
+// one's latency; a deeper ring runs one CTA per SM).  The region before the barriers
+// holds the ring, and after the walk the combine's partials (up to 4 heads x 32
+// partials x D floats, their m / l and denominators).
 template <int D>
+constexpr int default_stages() { return D == 128 ? 1 : 2; }
+
+template <int D, int STAGES_>
 struct Plan {
   static constexpr int BOXES = D / BOX_D;
   static constexpr int TSB = KEYS * D * 2;               // one tensor's stage bytes
-  static constexpr int STAGES = D == 128 ? 1 : 2;
+  static constexpr int STAGES = STAGES_;
   static constexpr int COMB = 4 * PARTIALS * D * 4 + 2 * 4 * PARTIALS * 4 + 64;
   static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
   static constexpr int SMEM = 1024 + REGION + STAGES * 8 + 64;
-  static_assert(2 * SMEM <= 227 * 1024, "two CTAs per SM must fit");
+  static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
+  static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
 };
 
 template <typename T>
@@ -567,11 +572,11 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
   return pack_rn<T>(lo, hi, a, b);
 }
 
-template <typename T, int D, int GH>
-__global__ void __launch_bounds__(64 * GH, 2)
+template <typename T, int D, int GH, int S>
+__global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
     sdpa_mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const Params p) {
-  using PL = Plan<D>;
+  using PL = Plan<D, S>;
   constexpr int NW = 2 * GH;         // warps: 16 MMA rows each
   constexpr int NT = 32 * NW;
   constexpr int NPW = 16 / GH;       // partials per warp
@@ -972,15 +977,15 @@ static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], co
   return encode_tiled16(map, base, 4, dims, strides, box, a.dtype);
 }
 
-template <typename T, int D, int GH>
+template <typename T, int D, int GH, int S = default_stages<D>()>
 static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  using PL = Plan<D>;
+  using PL = Plan<D, S>;
   CUtensorMap tk, tv;
   int st = kv_map<D>(&tk, a.k, a.ks, a);
   if (st) return st;
   st = kv_map<D>(&tv, a.v, a.vs, a);
   if (st) return st;
-  auto kern = sdpa_mma_kernel<T, D, GH>;
+  auto kern = sdpa_mma_kernel<T, D, GH, S>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        PL::SMEM);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa tc)");
@@ -990,17 +995,29 @@ static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   return cuda_status(cudaGetLastError(), "sdpa tc launch");
 }
 
-// Query heads per CTA: 4 (every K/V fragment serves four MMA row groups), or 2 or 1
-// when four would leave the GPU short of CTAs (fewer than two per SM: decode on a
-// head shard, small batches).  Each (head, partial) is one MMA row whose value depends
-// only on its own q row and the key columns, whatever the other rows hold, so the
-// heads-per-CTA count decides which CTA computes a row, never the row's bits.
+// Query heads per CTA (GH) and ring depth (S) for a grid of B * H / GH * qL CTAs.  Each
+// (head, partial) is one MMA row whose value depends only on its own q row and the key
+// columns, whatever the other rows hold, and the ring only stages keys, so both decide
+// which CTA computes a row and how its keys arrive -- never the row's bits.
+struct TcPlan {
+  int gh, stages;
+};
+
+static TcPlan tc_plan(const SdpaArgs& a, int sms) {
+  (void)a;
+  (void)sms;
+  return TcPlan{4, 0};
+}
+
 template <typename T, int D>
 static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  const int64_t want = 2LL * device_sm_count();
-  if (a.B * (a.H / 4) * a.qL >= want) return launch_gh<T, D, 4>(a, p, stream);
-  if (a.B * (a.H / 2) * a.qL >= want) return launch_gh<T, D, 2>(a, p, stream);
-  return launch_gh<T, D, 1>(a, p, stream);
+  const TcPlan pl = tc_plan(a, device_sm_count());
+  const bool deep = pl.stages > default_stages<D>();
+  switch (pl.gh) {
+    case 1: return deep ? launch_gh<T, D, 1, 3>(a, p, stream) : launch_gh<T, D, 1>(a, p, stream);
+    case 2: return deep ? launch_gh<T, D, 2, 3>(a, p, stream) : launch_gh<T, D, 2>(a, p, stream);
+    default: return deep ? launch_gh<T, D, 4, 3>(a, p, stream) : launch_gh<T, D, 4>(a, p, stream);
+  }
 }
 
 }  // namespace tcr

@@ -56,7 +56,8 @@ def test_mode_holds_for_function_compiled_inside(bi):
                               torch.nn.Linear(512, 128)).to("cuda", torch.float16)
     ref = randn((1, 256), torch.float16, 55, "cuda")
     pool = randn((16, 256), torch.float16, 56, "cuda")
-    with bi.batch_invariant_mode(strict=True):
+    # inference, as in the reference: the kernels are forward-only (no autograd formula)
+    with torch.no_grad(), bi.batch_invariant_mode(strict=True):
         fn = torch.compile(net)
         base = None
         for B in (1, 2, 3, 8, 16):
