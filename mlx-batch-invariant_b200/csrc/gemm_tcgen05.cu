@@ -95,7 +95,7 @@ struct RingCfg {
 using WideRing = RingCfg<BM, 6>;
 using ThinRing = RingCfg<16, 10>;
 constexpr int THIN_MAX_M = ThinRing::A_ROWS;
-constexpr int GROUP_M = 8;  // pair-tiles of M that consecutive tile indices sweep (L2 reuse)
+
 constexpr uint16_t PAIR_MASK = 0x3;
 
 // Error sites (code = site << 8 | reason).
@@ -118,14 +118,16 @@ struct Params {
   float alpha, beta;
   int has_bias;
   int tiles_m, tiles_n, num_tiles;
+  int group_m;    // pair-tiles of M that consecutive tile indices sweep (L2 reuse of W)
   GatherArgs gx;  // used when GATHER
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-  const int per_group = GROUP_M * tiles_n;
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m,
+                                            int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
   const int group = tile / per_group;
-  const int first_m = group * GROUP_M;
-  const int rows = min(tiles_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int rows = min(tiles_m - first_m, group_m);
   const int in_group = tile - group * per_group;
   tm = first_m + in_group % rows;
   tn = in_group / rows;
@@ -210,7 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       bool issued_any = false;
       for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
         int tm, tn;
-        tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -326,7 +328,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     int it = 0;
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++it) {
       int tm, tn;
-      tile_coords(tile, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(tile, p.tiles_m, p.tiles_n, p.group_m, tm, tn);
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       bool ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
@@ -644,6 +646,13 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
   return BI_OK;
 }
 
+// Raster of the persistent schedule: consecutive tile indices walk group_m pair-tiles
+// down M for one column tile before moving along N, so the pairs running at once share
+// a few W column slices in L2.  It decides which pair computes a tile, never a bit.
+static int group_m_for(int tiles_m) {
+  return tiles_m < 8 ? tiles_m : 8;
+}
+
 template <typename T, bool B_NK, bool GATHER, typename R>
 static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t stream) {
   CUtensorMap ma, mb;
@@ -675,6 +684,7 @@ static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t str
   p.tiles_m = static_cast<int>((g.M + 2 * BM - 1) / (2 * BM));
   p.tiles_n = static_cast<int>((g.N + R::BN - 1) / R::BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = group_m_for(p.tiles_m);
   if (gx != nullptr) {
     p.gx = *gx;
   } else {

@@ -1003,21 +1003,21 @@ struct TcPlan {
   int gh, stages;
 };
 
+// Four heads per CTA always (2 or 1 repeat the key-side MMAs per head: measured 1.5-4x
+// slower).  A grid with no more CTAs than SMs (decode on a head shard: 4 and 8 GPUs at
+// the bench shape) runs one CTA per SM with a 3-stage ring -- 4.9 vs 3.2 TB/s at
+// B = 64, H = 8, Hkv = 2 -- otherwise two CTAs per SM cover each other's latency.
 static TcPlan tc_plan(const SdpaArgs& a, int sms) {
-  (void)a;
-  (void)sms;
-  return TcPlan{4, 0};
+  const int64_t ctas = a.B * (a.H / 4) * a.qL;
+  return TcPlan{4, ctas <= sms ? 3 : 0};
 }
 
 template <typename T, int D>
 static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   const TcPlan pl = tc_plan(a, device_sm_count());
   const bool deep = pl.stages > default_stages<D>();
-  switch (pl.gh) {
-    case 1: return deep ? launch_gh<T, D, 1, 3>(a, p, stream) : launch_gh<T, D, 1>(a, p, stream);
-    case 2: return deep ? launch_gh<T, D, 2, 3>(a, p, stream) : launch_gh<T, D, 2>(a, p, stream);
-    default: return deep ? launch_gh<T, D, 4, 3>(a, p, stream) : launch_gh<T, D, 4>(a, p, stream);
-  }
+  (void)pl.gh;  // the kernel also builds for 1 or 2 heads per CTA; 4 is the one routed
+  return deep ? launch_gh<T, D, 4, 3>(a, p, stream) : launch_gh<T, D, 4>(a, p, stream);
 }
 
 }  // namespace tcr
