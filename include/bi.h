@@ -104,7 +104,8 @@ int bi_gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk,
  *          (reference _attention.py:80-86).
  *   out    (B, H, qL, V) with element strides out_strides[0..2], last dim contiguous.
  *
- * H % Hkv == 0; D and V multiples of 32 with D == V, D <= 256.  Each (query row,
+ * H % Hkv == 0; D and V multiples of 32, D, V <= 640 for fp16 / bf16 and D, V <= 384,
+ * D + V <= 768 for fp32 (else BI_ERR_UNSUPPORTED); D may differ from V.  Each (query row,
  * head) is reduced by one CTA over all N keys in 32 fixed strides (key i folds into
  * partial i % 32) with an fp32 online softmax and a fixed combine; there is no
  * split-KV and no route that depends on qL, B or N.  A row with no visible key

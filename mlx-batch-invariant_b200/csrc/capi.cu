@@ -180,8 +180,11 @@ int bi_sdpa(const void* q, const int64_t q_strides[3], const void* k, const int6
   if (D % 32 != 0 || V % 32 != 0) {
     return set_error(BI_ERR_INVALID, "head dimensions must be multiples of 32");
   }
-  if (D != V || D > 256) {
-    return set_error(BI_ERR_UNSUPPORTED, "built for D == V <= 256 (got D=%lld V=%lld)",
+  const bool f32 = dtype == BI_F32;
+  if ((f32 && (D > 384 || V > 384 || D + V > 768)) || (!f32 && (D > 640 || V > 640))) {
+    return set_error(BI_ERR_UNSUPPORTED,
+                     "head dims D=%lld V=%lld are not built (D, V <= 640 for 16-bit types; "
+                     "D, V <= 384 and D + V <= 768 for float32)",
                      static_cast<long long>(D), static_cast<long long>(V));
   }
   if (mask_mode < 0 || mask_mode > 2) return set_error(BI_ERR_INVALID, "mask_mode must be 0..2");

@@ -67,6 +67,7 @@ struct Params {
   const void* sinks;
   float scale;
   int B, H, Hkv, qL, N;
+  int D, V;  // head dims (the generic kernel reads them; the others have them built in)
   void* out;
   int64_t os0, os1, os2;
 };
@@ -461,6 +462,296 @@ __global__ void __launch_bounds__(PARTIALS * LP, (PARTIALS * LP <= 256 ? BI_SDPA
         static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
     }
   }
+}
+
+
+// ---------------------------------------------------------------------------
+// Generic head dims: D != V, or either above 256 (multiples of 32; D, V <= 640 for
+// 16-bit types -- MLA's 576 / 512 among them -- and D, V <= 384, D + V <= 768 for
+// float32).  The same fold as sdpa_kernel, one query
+// head per CTA, with the head dims known only at run time:
+//   * a partial is 16 threads; thread `sub` holds elements (2c*16 + 2 sub, +1), c < D/32,
+//     of q and k (and likewise of v and o with V), so each row is read as 16
+//     consecutive 4- or 8-byte words per pair of elements;
+//   * the q.k dot of a thread runs the four fp32 chains of sdpa_kernel (its k-th
+//     element to chain (k/2 % 2)*2 + k%2), summed (c0 + c1) + (c2 + c3), then a
+//     xor-butterfly over the 16 threads -- the lane split bi_oracle.c follows with
+//     lanes = 16 and two-element vectors;
+//   * K and V rows stream through a ring of 32-key stages (one key per partial).
+// ---------------------------------------------------------------------------
+constexpr int GEN_LP = 16;
+constexpr int GEN_NT = PARTIALS * GEN_LP;  // 512 threads
+
+// Elements e and e + 1 (e even) of a row in shared memory, widened to an fp32 pair.
+template <typename T>
+__device__ __forceinline__ f2 load_pair(const T* row, int e) {
+  if constexpr (sizeof(T) == 4) {
+    const float2 w = *reinterpret_cast<const float2*>(row + e);
+    return pack2(w.x, w.y);
+  } else if constexpr (dtype_of<T>::value == 2) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + e);
+    return f2{static_cast<uint64_t>(w << 16) | (static_cast<uint64_t>(w & 0xffff0000u) << 32)};
+  } else {
+    const float2 fl = __half22float2(*reinterpret_cast<const __half2*>(row + e));
+    return pack2(fl.x, fl.y);
+  }
+}
+
+template <typename T, int EMAX, int EVMAX>
+__global__ void __launch_bounds__(GEN_NT, 1) sdpa_generic_kernel(const Params p, int stages) {
+  constexpr int NW = GEN_NT / 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int D = p.D, V = p.V;
+  const int E2 = D / 32, EV2 = V / 32;  // element pairs per thread
+  T* sK = reinterpret_cast<T*>(smem);
+  T* sV = sK + static_cast<int64_t>(stages) * PARTIALS * D;
+  uint8_t* tail = reinterpret_cast<uint8_t*>(sV + static_cast<int64_t>(stages) * PARTIALS * V);
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(tail) + 7) & ~static_cast<uintptr_t>(7));
+  int* done_count = reinterpret_cast<int*>(full + stages);  // [stages]
+  int* issued_count = done_count + stages;
+  volatile int* abort_flag = issued_count + 1;
+  float* comb_m = reinterpret_cast<float*>(done_count + stages + 4);  // [PARTIALS]
+  float* comb_l = comb_m + PARTIALS;                                  // [PARTIALS + 1]
+  float* comb_o = reinterpret_cast<float*>(smem);  // [PARTIALS][V], after the walk
+
+  const int tid = threadIdx.x;
+  const int part = tid / GEN_LP;
+  const int sub = tid % GEN_LP;
+  const int lane = tid & 31;
+
+  int idx = blockIdx.x;
+  const int s = idx % p.qL;
+  idx /= p.qL;
+  const int h = idx % p.H;
+  const int b = idx / p.H;
+  const int kvh = h / (p.H / p.Hkv);
+
+  int64_t kmax = p.N;
+  if (p.mask_mode == 1) {
+    const int64_t last = p.causal_offset + s;
+    kmax = last < 0 ? 0 : (last + 1 < p.N ? last + 1 : p.N);
+  }
+  const int nblocks = static_cast<int>((kmax + PARTIALS - 1) / PARTIALS);
+
+  const T* Kb = static_cast<const T*>(p.k) + static_cast<int64_t>(b) * p.ks0 +
+                static_cast<int64_t>(kvh) * p.ks1;
+  const T* Vb = static_cast<const T*>(p.v) + static_cast<int64_t>(b) * p.vs0 +
+                static_cast<int64_t>(kvh) * p.vs1;
+  const T* Mk = static_cast<const T*>(p.mask);
+  const T* mrow = Mk == nullptr ? nullptr
+                                : Mk + static_cast<int64_t>(b) * p.ms0 +
+                                      static_cast<int64_t>(h) * p.ms1 + static_cast<int64_t>(s) * p.ms2;
+  const T* qrow = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.qs0 +
+                  static_cast<int64_t>(h) * p.qs1 + static_cast<int64_t>(s) * p.qs2;
+
+  // q pre-scaled in fp32; o zero.  Pair c of the thread: elements 2 (c*16 + sub), +1.
+  f2 qv[EMAX / 2], o[EVMAX / 2];
+  const f2 sc = pack2(p.scale, p.scale);
+#pragma unroll
+  for (int c = 0; c < EMAX / 2; ++c) {
+    if (c < E2) {
+      const int e = 2 * (c * GEN_LP + sub);
+      qv[c] = mul2(sc, pack2(to_f32(qrow[e]), to_f32(qrow[e + 1])));
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < EVMAX / 2; ++c) o[c] = f2{0};
+  float m = -3.40282347e+38f;
+  float l = 0.f;
+  const T* Sk = static_cast<const T*>(p.sinks);
+  if (Sk != nullptr && part == 0) {
+    m = to_f32(Sk[h]);
+    l = 1.f;
+  }
+
+  const uint32_t krow_bytes = static_cast<uint32_t>(D) * sizeof(T);
+  const uint32_t vrow_bytes = static_cast<uint32_t>(V) * sizeof(T);
+  auto issue = [&](int blk) {
+    const int st = blk % stages;
+    const int64_t i0 = static_cast<int64_t>(blk) * PARTIALS;
+    const int64_t rows = (kmax - i0) < PARTIALS ? (kmax - i0) : PARTIALS;
+    const uint32_t kb = static_cast<uint32_t>(rows) * krow_bytes;
+    const uint32_t vb = static_cast<uint32_t>(rows) * vrow_bytes;
+    mbar_arrive_expect_tx(&full[st], kb + vb);
+    bulk_load(sK + static_cast<int64_t>(st) * PARTIALS * D, Kb + i0 * D, kb, &full[st]);
+    bulk_load(sV + static_cast<int64_t>(st) * PARTIALS * V, Vb + i0 * V, vb, &full[st]);
+  };
+
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) {
+      mbar_init(&full[st], 1);
+      done_count[st] = 0;
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    int n0 = 0;
+    for (; n0 < stages && n0 < nblocks; ++n0) issue(n0);
+    *issued_count = n0;
+  }
+  __syncthreads();
+
+  bool aborted = false;
+  for (int t = 0; t < nblocks; ++t) {
+    const int st = t % stages;
+    bool ok = mbar_wait(&full[st], static_cast<uint32_t>((t / stages) & 1), abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (3u << 8) | kErrReasonTimeout);
+      }
+      aborted = true;
+      break;
+    }
+    const int64_t i = static_cast<int64_t>(t) * PARTIALS + part;  // this partial's key
+    const bool in_range = i < kmax;
+    const T* krow = sK + (static_cast<int64_t>(st) * PARTIALS + part) * D;
+    // four fp32 chains: pairs c even -> acc[0], c odd -> acc[1]
+    f2 acc[2] = {f2{0}, f2{0}};
+#pragma unroll
+    for (int c = 0; c < EMAX / 2; ++c) {
+      if (c < E2) {
+        acc[c & 1] = fma2(qv[c], load_pair<T>(krow, 2 * (c * GEN_LP + sub)), acc[c & 1]);
+      }
+    }
+    float dot = __fadd_rn(__fadd_rn(lo_of(acc[0]), hi_of(acc[0])),
+                          __fadd_rn(lo_of(acc[1]), hi_of(acc[1])));
+#pragma unroll
+    for (int off = GEN_LP / 2; off >= 1; off >>= 1) {
+      dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
+    }
+    // scalar online-softmax step (every thread of the partial computes the same values)
+    float bias = 0.f;
+    bool use = in_range;
+    if (p.mask_mode == 2 && in_range) {
+      bias = to_f32(mrow[i]);
+      use = bias > -3.0e38f;
+    }
+    if (use) {
+      const float score = __fadd_rn(dot, bias);
+      float f = 1.f, ex;
+      if (score > m) {
+        f = expf(__fsub_rn(m, score));
+        m = score;
+        ex = 1.0f;
+        l = __fmaf_rn(l, f, 1.0f);
+      } else {
+        ex = expf(__fsub_rn(score, m));
+        l = __fadd_rn(l, ex);
+      }
+      const T* vrow = sV + (static_cast<int64_t>(st) * PARTIALS + part) * V;
+      const f2 e_2 = pack2(ex, ex);
+      const f2 f_2 = pack2(f, f);
+#pragma unroll
+      for (int c = 0; c < EVMAX / 2; ++c) {
+        if (c < EV2) {
+          if (f != 1.0f) o[c] = mul2(o[c], f_2);
+          o[c] = fma2(e_2, load_pair<T>(vrow, 2 * (c * GEN_LP + sub)), o[c]);
+        }
+      }
+    }
+    // The last warp to finish with this stage refills it with block t + stages.
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&done_count[st], 1) == NW - 1) {
+        __threadfence_block();
+        done_count[st] = 0;
+        if (t + stages < nblocks && !*abort_flag) {
+          fence_proxy_async_smem();
+          issue(t + stages);
+          atomicMax(issued_count, t + stages + 1);
+        }
+      }
+    }
+  }
+  if (__syncthreads_or(aborted)) {
+    if (tid == 0) {
+      const int issued = *issued_count;
+      for (int blk = issued - stages < 0 ? 0 : issued - stages; blk < issued; ++blk) {
+        mbar_wait(&full[blk % stages], static_cast<uint32_t>((blk / stages) & 1), nullptr);
+      }
+    }
+    return;
+  }
+  __syncthreads();  // every stage consumed: the ring is free for the combine
+
+#pragma unroll
+  for (int c = 0; c < EVMAX / 2; ++c) {
+    if (c < EV2) {
+      const int e = 2 * (c * GEN_LP + sub);
+      *reinterpret_cast<float2*>(&comb_o[part * V + e]) = make_float2(lo_of(o[c]), hi_of(o[c]));
+    }
+  }
+  if (sub == 0) {
+    comb_m[part] = m;
+    comb_l[part] = l;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const float ls = combine_weights(comb_m, comb_l, tid);  // comb_m now holds f_q
+    if (tid == 0) comb_l[PARTIALS] = ls;
+  }
+  __syncthreads();
+  const float lsum = comb_l[PARTIALS];
+  T* O = static_cast<T*>(p.out);
+  for (int j = tid; j < V; j += GEN_NT) {
+    float a = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < PARTIALS; ++q) a = __fmaf_rn(comb_o[q * V + j], comb_m[q], a);
+    const float res = lsum == 0.f ? a : __fdiv_rn(a, lsum);
+    O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h) * p.os1 +
+      static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
+  }
+}
+
+// Shared memory of the generic kernel at `stages` ring stages (the combine reuses the
+// ring, so the ring is made at least as large as its 32 x V floats).
+static int64_t generic_smem(int64_t D, int64_t V, int64_t es, int stages) {
+  int64_t ring = static_cast<int64_t>(stages) * PARTIALS * (D + V) * es;
+  const int64_t comb = static_cast<int64_t>(PARTIALS) * V * 4;
+  if (ring < comb) ring = comb;
+  return ring + 8 + static_cast<int64_t>(stages) * 8 + 4 * (stages + 4) + (2 * PARTIALS + 1) * 4;
+}
+
+template <typename T, int EMAX, int EVMAX>
+static int launch_generic_t(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  const int64_t es = sizeof(T);
+  const int64_t stage_bytes = PARTIALS * (a.D + a.V) * es;
+  int stages = static_cast<int>((160 * 1024) / stage_bytes);
+  if (stages > 4) stages = 4;
+  if (stages < 2) stages = 2;
+  const int64_t smem = generic_smem(a.D, a.V, es, stages);
+  if (smem > 227 * 1024) {
+    return set_error(BI_ERR_UNSUPPORTED, "head dims D=%lld V=%lld are too large for one CTA",
+                     static_cast<long long>(a.D), static_cast<long long>(a.V));
+  }
+  auto kern = sdpa_generic_kernel<T, EMAX, EVMAX>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa generic)");
+  const int64_t blocks = a.B * a.H * a.qL;
+  if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "too many attention rows");
+  kern<<<static_cast<unsigned>(blocks), GEN_NT, static_cast<size_t>(smem), stream>>>(p, stages);
+  return cuda_status(cudaGetLastError(), "sdpa generic launch");
+}
+
+// Register arrays sized for the head dims: up to 256 or up to 640 elements.
+template <typename T>
+static int launch_generic(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  const int64_t lim = sizeof(T) == 4 ? 384 : 640;
+  if (a.D > lim || a.V > lim || (sizeof(T) == 4 && a.D + a.V > 768)) {
+    return set_error(BI_ERR_UNSUPPORTED,
+                     "head dims D=%lld V=%lld are not built (multiples of 32; D, V <= 640 for "
+                     "16-bit types; D, V <= 384 and D + V <= 768 for float32)",
+                     static_cast<long long>(a.D), static_cast<long long>(a.V));
+  }
+  const bool wd = a.D > 256, wv = a.V > 256;
+  if (!wd && !wv) return launch_generic_t<T, 16, 16>(a, p, stream);
+  if (wd && !wv) return launch_generic_t<T, 40, 16>(a, p, stream);
+  if (!wd && wv) return launch_generic_t<T, 16, 40>(a, p, stream);
+  return launch_generic_t<T, 40, 40>(a, p, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -1029,6 +1320,7 @@ static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
 // a token's bits are the same in decode and in any chunked prefill.
 template <typename T>
 static int launch_t(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  if (a.D != a.V || a.D > 256) return launch_generic<T>(a, p, stream);
   if constexpr (sizeof(T) == 2) {
     if ((a.H / a.Hkv) % 4 == 0) {
       if (a.D == 64) return tcr::launch<T, 64>(a, p, stream);
@@ -1077,6 +1369,8 @@ int launch_sdpa(const SdpaArgs& a, cudaStream_t stream) {
   p.Hkv = static_cast<int>(a.Hkv);
   p.qL = static_cast<int>(a.qL);
   p.N = static_cast<int>(a.N);
+  p.D = static_cast<int>(a.D);
+  p.V = static_cast<int>(a.V);
   p.out = a.out;
   p.os0 = a.os[0];
   p.os1 = a.os[1];

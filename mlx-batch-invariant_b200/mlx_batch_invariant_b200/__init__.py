@@ -22,7 +22,7 @@ import torch.nn.functional as F
 
 from . import _ops  # noqa: F401  (registers mlx_bi::gemm and mlx_bi::sdpa)
 from ._attention import _mask_args, _sdpa, scaled_dot_product_attention
-from ._attention import MAX_HEAD_DIM
+from ._attention import head_dims_built
 from ._gemm import QUANT_BITS, SIMT_TILE, TILE, addmm, linear, matmul, quantized_linear, tile_for
 
 __all__ = [
@@ -157,7 +157,8 @@ def batch_invariant_mode(strict=True):
             return stock()
         B, H, qL, D = query.shape
         Hkv, N, V = key.shape[1], key.shape[2], value.shape[-1]
-        if D % 32 or V % 32 or D != V or D > MAX_HEAD_DIM or Hkv == 0 or H % Hkv:
+        if (D % 32 or V % 32 or not head_dims_built(D, V, query.dtype) or Hkv == 0
+                or H % Hkv):
             return stock()
         if H != Hkv and not enable_gqa:
             # stock torch broadcasts a single KV head here; that call is not invariant

@@ -16,7 +16,15 @@ from . import _lib
 
 BN = 32  # partial softmax states per row -- also the stride of the key walk
 BD = 32  # head dims must be multiples of this (reference _attention.py:29-30)
-MAX_HEAD_DIM = 256  # largest head dim this build has a kernel for (D == V)
+MAX_HEAD_DIM = 640  # largest head dim this build has a kernel for (16-bit types)
+MAX_HEAD_DIM_F32 = 384  # float32: D, V <= 384 and D + V <= 768
+
+
+def head_dims_built(D, V, dtype):
+    """Whether libbi.so has a kernel for head dims (D, V) (multiples of 32) in dtype."""
+    if dtype == torch.float32:
+        return D <= MAX_HEAD_DIM_F32 and V <= MAX_HEAD_DIM_F32 and D + V <= 2 * MAX_HEAD_DIM_F32
+    return D <= MAX_HEAD_DIM and V <= MAX_HEAD_DIM
 
 
 def _mask_args(mask, B, H, qL, N, dtype):
@@ -127,9 +135,11 @@ def scaled_dot_product_attention(q, k, v, *, scale=None, mask=None, sinks=None):
         raise ValueError("head count %d is not a multiple of kv head count %d" % (H, Hkv))
     if D % BD or V % BD:
         raise ValueError("head dimensions must be multiples of %d, got D=%d V=%d" % (BD, D, V))
-    if D != V or D > MAX_HEAD_DIM:
+    if not head_dims_built(D, V, q.dtype):
         raise NotImplementedError(
-            "attention with D=%d, V=%d is not built (D == V <= %d)" % (D, V, MAX_HEAD_DIM))
+            "attention with D=%d, V=%d in %s is not built (D, V <= %d for 16-bit types; "
+            "D, V <= %d and D + V <= %d for float32)"
+            % (D, V, q.dtype, MAX_HEAD_DIM, MAX_HEAD_DIM_F32, 2 * MAX_HEAD_DIM_F32))
     _lib.dtype_code(q.dtype)
 
     scale = 1.0 / math.sqrt(D) if scale is None else float(scale)

@@ -166,15 +166,16 @@ void oracle_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, const v
 
 /*
  * Strides are in elements for (b, h, s) of q/out/mask and (b, h) of k/v; the last
- * dimension of every tensor is contiguous and each (N, D) head block of k and v is
+ * dimension of every tensor is contiguous and each head block of k and v is
  * row-contiguous.  lanes: threads a key row is split over (a power of two dividing
- * D, leaving an even count per lane); D == V.
+ * D, leaving an even count per lane); here D == V (oracle_sdpa_ex takes V apart).
  */
 void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                     const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
                     int mask_mode, int64_t causal_offset, const void* sinks, float scale,
-                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt,
-                    void* out, const int64_t* os, int out_dt, int lanes, int nthreads);
+                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D,
+                    int64_t V, int dt, void* out, const int64_t* os, int out_dt, int lanes,
+                    int per_elems, int nthreads);
 
 void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                  const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
@@ -182,16 +183,21 @@ void oracle_sdpa(const void* q, const int64_t* qs, const void* k, const int64_t*
                  int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt, void* out,
                  const int64_t* os, int lanes, int nthreads) {
   oracle_sdpa_ex(q, qs, k, ks, v, vs, mask, ms, mask_mode, causal_offset, sinks, scale, B, H,
-                 Hkv, qL, N, D, dt, out, os, dt, lanes, nthreads);
+                 Hkv, qL, N, D, D, dt, out, os, dt, lanes, 0, nthreads);
 }
 
-/* As oracle_sdpa, with the output written as out_dt: OR_F32 keeps the fold's fp32
- * result before the final rounding to the input type (for elementwise error bars). */
+/* As oracle_sdpa, with v and the output V wide (V may differ from D), the output
+ * written as out_dt (OR_F32 keeps the fold's fp32 result before the final rounding to
+ * the input type, for elementwise error bars), and per_elems > 0 fixing the elements
+ * per vector of a lane's share of a q / k row (0: the widest of 16, 8 or 4 bytes that
+ * divides the share, as libbi.so's kernels for D == V <= 256 take it; libbi.so's
+ * kernel for other head dims uses 16 lanes and 2-element vectors). */
 void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64_t* ks,
                     const void* v, const int64_t* vs, const void* mask, const int64_t* ms,
                     int mask_mode, int64_t causal_offset, const void* sinks, float scale,
-                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D, int dt,
-                    void* out, const int64_t* os, int out_dt, int lanes, int nthreads) {
+                    int64_t B, int64_t H, int64_t Hkv, int64_t qL, int64_t N, int64_t D,
+                    int64_t V, int dt, void* out, const int64_t* os, int out_dt, int lanes,
+                    int per_elems, int nthreads) {
   const int64_t G = H / Hkv;
   const int64_t E = D / lanes;
   /* a lane's share of a row: vectors of W bytes (16, 8 or 4, whichever divides its
@@ -199,7 +205,7 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
      element (c*lanes + t)*per */
   const int64_t es = dt == OR_F32 ? 4 : 2;
   const int64_t vbytes = (E * es) % 16 == 0 ? 16 : ((E * es) % 8 == 0 ? 8 : 4);
-  const int64_t per = vbytes / es;
+  const int64_t per = per_elems > 0 ? per_elems : vbytes / es;
   const int64_t rows = B * H * qL;
 #ifdef _OPENMP
   if (nthreads > 0) omp_set_num_threads(nthreads);
@@ -208,8 +214,8 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
   {
     float* qv = (float*)malloc(sizeof(float) * D);
     float* kf = (float*)malloc(sizeof(float) * D);
-    float* vf = (float*)malloc(sizeof(float) * D);
-    float* o = (float*)malloc(sizeof(float) * PARTIALS * D);
+    float* vf = (float*)malloc(sizeof(float) * V);
+    float* o = (float*)malloc(sizeof(float) * PARTIALS * V);
     float* part = (float*)malloc(sizeof(float) * lanes);
     float* tmp = (float*)malloc(sizeof(float) * lanes);
     float m[PARTIALS], l[PARTIALS];
@@ -225,7 +231,7 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
       for (int p = 0; p < PARTIALS; ++p) {
         m[p] = -3.40282347e+38f;
         l[p] = 0.0f;
-        for (int64_t j = 0; j < D; ++j) o[p * D + j] = 0.0f;
+        for (int64_t j = 0; j < V; ++j) o[p * V + j] = 0.0f;
       }
       if (sinks) {
         m[0] = load_elem(sinks, h, dt);
@@ -247,10 +253,8 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
           use = bias > -3.0e38f;
         }
         if (!use) continue;
-        for (int64_t j = 0; j < D; ++j) {
-          kf[j] = load_elem(k, kb + i * D + j, dt);
-          vf[j] = load_elem(v, vb + i * D + j, dt);
-        }
+        for (int64_t j = 0; j < D; ++j) kf[j] = load_elem(k, kb + i * D + j, dt);
+        for (int64_t j = 0; j < V; ++j) vf[j] = load_elem(v, vb + i * V + j, dt);
         for (int t = 0; t < lanes; ++t) {
           /* four chains -- the lane's e-th element (row element ((e/per)*lanes + t)*per
              + e%per) goes to chain (e/2 % 2)*2 + e%2 -- summed (c0+c1)+(c2+c3) */
@@ -271,9 +275,9 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
         const float f = expf(m[p] - mnew);
         const float ex = expf(score - mnew);
         l[p] = fmaf(l[p], f, ex);
-        for (int64_t j = 0; j < D; ++j) {
-          const float scaled = o[p * D + j] * f;
-          o[p * D + j] = fmaf(ex, vf[j], scaled);
+        for (int64_t j = 0; j < V; ++j) {
+          const float scaled = o[p * V + j] * f;
+          o[p * V + j] = fmaf(ex, vf[j], scaled);
         }
         m[p] = mnew;
       }
@@ -285,9 +289,9 @@ void oracle_sdpa_ex(const void* q, const int64_t* qs, const void* k, const int64
         fp[p] = expf(m[p] - mx);
         lsum = fmaf(l[p], fp[p], lsum);
       }
-      for (int64_t j = 0; j < D; ++j) {
+      for (int64_t j = 0; j < V; ++j) {
         float acc = 0.0f;
-        for (int p = 0; p < PARTIALS; ++p) acc = fmaf(o[p * D + j], fp[p], acc);
+        for (int p = 0; p < PARTIALS; ++p) acc = fmaf(o[p * V + j], fp[p], acc);
         const float res = lsum == 0.0f ? acc : acc / lsum;
         store_elem(out, b * os[0] + h * os[1] + s * os[2] + j, res, out_dt);
       }

@@ -54,9 +54,9 @@ def lib():
                                   vp, _i64p, ctypes.c_int, ctypes.c_int]
         L.oracle_sdpa_ex.restype = None
         L.oracle_sdpa_ex.argtypes = [vp, _i64p, vp, _i64p, vp, _i64p, vp, _i64p, ctypes.c_int,
-                                     i64, vp, ctypes.c_float, i64, i64, i64, i64, i64, i64,
+                                     i64, vp, ctypes.c_float, i64, i64, i64, i64, i64, i64, i64,
                                      ctypes.c_int, vp, _i64p, ctypes.c_int, ctypes.c_int,
-                                     ctypes.c_int]
+                                     ctypes.c_int, ctypes.c_int]
         L.oracle_round.restype = ctypes.c_float
         L.oracle_round.argtypes = [ctypes.c_float, ctypes.c_int]
         _lib = L
@@ -89,8 +89,15 @@ def gemm(a, b, bias=None, b_is_nk=False, alpha=1.0, beta=1.0, threads=0):
     return out
 
 
+def generic_route(D, V):
+    """Whether bi_sdpa takes its kernel for other head dims (D != V or D > 256): 16
+    lanes per key row and 2-element vectors, whatever the dtype."""
+    return D != V or D > 256
+
+
 def lanes_for(D, dtype):
-    """Threads a key row is split over in bi_sdpa (a function of D and dtype only)."""
+    """Threads a key row is split over in bi_sdpa (a function of D and dtype only),
+    for D == V <= 256."""
     es = np.dtype(dtype).itemsize
     lp = max(1, min(16, (D * es) // 32))
     p2 = 1
@@ -112,10 +119,12 @@ def sdpa(q, k, v, mask=None, mask_mode=0, causal_offset=0, sinks=None, scale=Non
     dt = q.dtype
     B, H, qL, D = q.shape
     _, Hkv, N, V = v.shape
-    assert D == V
     if scale is None:
         scale = 1.0 / np.sqrt(D)
-    if lanes is None:
+    per = 0
+    if generic_route(D, V):
+        lanes, per = 16, 2
+    elif lanes is None:
         lanes = lanes_for(D, dt)
     odt = np.dtype(out_dtype) if out_dtype is not None else dt
     out = np.empty((B, H, qL, V), dtype=odt)
@@ -130,11 +139,12 @@ def sdpa(q, k, v, mask=None, mask_mode=0, causal_offset=0, sinks=None, scale=Non
         sinks = np.ascontiguousarray(sinks.astype(dt))
     qs = [H * qL * D, qL * D, D]
     ks = [Hkv * N * D, N * D]
+    vs = [Hkv * N * V, N * V]
     os_ = [H * qL * V, qL * V, V]
-    lib().oracle_sdpa_ex(_ptr(q), _i64s(qs), _ptr(k), _i64s(ks), _ptr(v), _i64s(ks),
+    lib().oracle_sdpa_ex(_ptr(q), _i64s(qs), _ptr(k), _i64s(ks), _ptr(v), _i64s(vs),
                          _ptr(mask), _i64s(ms), mask_mode, causal_offset, _ptr(sinks),
-                         float(scale), B, H, Hkv, qL, N, D, CODES[dt], _ptr(out), _i64s(os_),
-                         CODES[odt], lanes, threads)
+                         float(scale), B, H, Hkv, qL, N, D, V, CODES[dt], _ptr(out), _i64s(os_),
+                         CODES[odt], lanes, per, threads)
     return out
 
 

@@ -81,9 +81,10 @@ def ulp_of(x, dtype):
     return 2.0 ** (np.floor(np.log2(mag)) - _MANT[dtype])
 
 
-def sdpa_tc_route(dtype, H, Hkv, D):
+def sdpa_tc_route(dtype, H, Hkv, D, V=None):
     """Whether bi_sdpa takes its tensor-core route for these shapes."""
-    return dtype != torch.float32 and (H // Hkv) % 4 == 0 and D in (64, 128)
+    V = D if V is None else V
+    return dtype != torch.float32 and (H // Hkv) % 4 == 0 and D in (64, 128) and V == D
 
 
 def attn_worst(got, q, k, v, mask_mode=0, mask=None, causal_offset=0, sinks=None):
@@ -109,7 +110,7 @@ def attn_worst(got, q, k, v, mask_mode=0, mask=None, causal_offset=0, sinks=None
     absv = orc.attention_f64(q32, k32, np.abs(v32), mask=m64, sinks=s32)
     g = to_np(got).astype(np.float64)
     w = w.astype(np.float64)
-    tau = 2.0 ** -16 if sdpa_tc_route(dtype, H, Hkv, D) else 2.0 ** -20
+    tau = 2.0 ** -16 if sdpa_tc_route(dtype, H, Hkv, D, v.shape[3]) else 2.0 ** -20
     if dtype == torch.float32:
         bar = 2 * ulp_of(w, dtype) + tau * absv
     else:

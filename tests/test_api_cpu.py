@@ -71,7 +71,8 @@ def test_sdpa_argument_errors_are_status_codes():
                                        1, H, Hkv, 1, 16, D, V, 2, None, z3, None)
     assert L.bi_sdpa(*args(8, 3, 64, 64, 0)) == -1  # H % Hkv
     assert L.bi_sdpa(*args(8, 4, 48, 48, 0)) == -1  # D % 32
-    assert L.bi_sdpa(*args(8, 4, 64, 128, 0)) == -2  # D != V not built
+    assert L.bi_sdpa(*args(8, 4, 672, 512, 0)) == -2  # head dims above 640 not built
+    assert L.bi_sdpa(*args(8, 4, 64, 128, 0)) == -1  # D != V is built: fails on null q
     assert L.bi_sdpa(*args(8, 4, 64, 64, 3)) == -1  # mask mode
     assert L.bi_sdpa(*args(8, 4, 64, 64, 2)) == -1  # mode 2 without a mask
 
@@ -118,7 +119,9 @@ def test_sdpa_validation_errors():
         bi.scaled_dot_product_attention(q, k, v, mask=torch.zeros(1, 1, 3, 10))
     with pytest.raises(ValueError, match="sinks must have shape"):
         bi.scaled_dot_product_attention(q, k, v, sinks=torch.zeros(4))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(NotImplementedError):  # head dims above 640 are not built
+        bi.scaled_dot_product_attention(q, k, torch.zeros(1, 4, 10, 672))
+    with pytest.raises(ValueError, match="CUDA tensors"):  # D != V is built (CUDA only)
         bi.scaled_dot_product_attention(q, k, torch.zeros(1, 4, 10, 128))
     with pytest.raises(ValueError, match="CUDA tensors"):
         bi.scaled_dot_product_attention(q, k, v)

@@ -260,3 +260,20 @@ def test_elementwise_attention_bar_accepts_the_rounded_fold(dt):
     bad = ot.clone().float()
     bad.view(-1)[5] = bad.view(-1)[5] * (1 + 2.0 ** -6)
     assert attn_worst(bad.to(dtype), q, k, v, mask_mode=1, causal_offset=297) > 1.0
+
+
+@pytest.mark.parametrize("D,V", [(192, 128), (64, 128), (576, 512)])
+def test_oracle_sdpa_with_v_wider_or_narrower_than_d(D, V):
+    """Head dims the reference takes (any multiples of 32, D != V allowed): the oracle's
+    fold against float64, within the reference's float32 bar."""
+    rng = np.random.default_rng(D + V)
+    q = rng.standard_normal((1, 4, 3, D), dtype=np.float32)
+    k = rng.standard_normal((1, 2, 200, D), dtype=np.float32)
+    v = rng.standard_normal((1, 2, 200, V), dtype=np.float32)
+    got = orc.sdpa(q, k, v, mask_mode=1, causal_offset=197)
+    i = np.arange(200)[None, :]
+    s = np.arange(3)[:, None]
+    m = np.where(i <= 197 + s, 0.0, -np.inf)[None, None]
+    want = orc.attention_f64(q, k, v, mask=m)
+    assert got.shape == (1, 4, 3, V)
+    assert orc.rel_error(got, want) < 2e-6

@@ -333,3 +333,96 @@ def test_stock_sdpa_is_query_variant_control():
             if any(int((o != outs[0]).sum()) for o in outs[1:]):
                 found.append((dtype, H, N, D))
     assert found, "stock torch SDPA looks query-length invariant everywhere"
+
+
+# (H, Hkv, qL, N, D, V): head dims the generic kernel takes -- D != V (a DeepSeek-style
+# 192 / 128, MLA's absorbed 576 / 512) or above 256.
+GENERIC = [(8, 2, 3, 300, 192, 128), (4, 4, 2, 130, 64, 128), (8, 8, 1, 257, 128, 64),
+           (4, 2, 5, 200, 320, 320), (4, 1, 2, 150, 96, 288), (2, 1, 3, 100, 576, 512),
+           (2, 2, 2, 64, 512, 512), (4, 2, 2, 90, 640, 640)]
+
+
+def _generic_built(dtype, D, V):
+    if dtype == torch.float32:
+        return D <= 384 and V <= 384 and D + V <= 768
+    return D <= 640 and V <= 640
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("maskkind", ["none", "causal", "additive", "bool", "sinks"])
+def test_generic_head_dims_parity_against_oracle(bi, dtype, maskkind):
+    """D != V and head dims above 256 (the reference takes any multiples of 32,
+    _attention.py:216-223): elementwise against the oracle's fold with the generic
+    kernel's lane split (16 lanes, 2-element vectors)."""
+    ran = 0
+    for (H, Hkv, qL, N, D, V) in GENERIC:
+        if not _generic_built(dtype, D, V):
+            continue
+        q = randn((2, H, qL, D), dtype, 71, "cuda")
+        k = randn((2, Hkv, N, D), dtype, 72, "cuda")
+        v = randn((2, Hkv, N, V), dtype, 73, "cuda")
+        sinks = randn((H,), dtype, 74, "cuda") if maskkind == "sinks" else None
+        if maskkind == "causal":
+            y = bi.scaled_dot_product_attention(q, k, v, mask="causal")
+            worst = attn_worst(y, q, k, v, mask_mode=1, causal_offset=N - qL)
+        elif maskkind in ("additive", "bool"):
+            if maskkind == "additive":
+                mask = randn((1, 1, qL, N), dtype, 75, "cuda")
+            else:
+                g = torch.Generator().manual_seed(76)
+                mask = (torch.rand(2, 1, qL, N, generator=g) > 0.1).cuda()
+            y = bi.scaled_dot_product_attention(q, k, v, mask=mask)
+            worst = attn_worst(y, q, k, v, mask_mode=2, mask=torch.from_numpy(
+                np.asarray(_np_mask(mask, dtype), dtype=np.float32)).to(dtype))
+        else:
+            y = bi.scaled_dot_product_attention(q, k, v, sinks=sinks)
+            worst = attn_worst(y, q, k, v, sinks=sinks)
+        assert y.shape == (2, H, qL, V)
+        assert worst <= 1.0, (dtype, maskkind, H, Hkv, qL, N, D, V, worst)
+        ran += 1
+    assert ran >= 5
+    assert bi._lib.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_generic_head_dims_are_query_length_and_batch_invariant(bi, dtype):
+    """The generic kernel keeps the fold's contract: a query's bits do not depend on
+    the other queries of the call or on the batch around it; a masked extra key is a
+    no-op."""
+    shapes = [(8, 2, 1000, 192, 128)] + ([(4, 1, 700, 576, 512)] if dtype != torch.float32
+                                          else [(4, 1, 700, 320, 320)])
+    for H, Hkv, N, D, V in shapes:
+        k = randn((1, Hkv, N, D), dtype, 81, "cuda")
+        v = randn((1, Hkv, N, V), dtype, 82, "cuda")
+        qf = randn((1, H, 17, D), dtype, 83, "cuda")
+        base = None
+        for qL in (1, 2, 7, 9, 17):
+            y = bi.scaled_dot_product_attention(qf[:, :, 17 - qL:].contiguous(), k, v,
+                                                mask="causal")
+            got = bits(y[:, :, -1])
+            if base is None:
+                base = got
+            else:
+                assert np.array_equal(got, base), (D, V, qL)
+        # batch: the same row in slot 0 of a batch of 3
+        kb = torch.cat([k, randn((2, Hkv, N, D), dtype, 84, "cuda")])
+        vb = torch.cat([v, randn((2, Hkv, N, V), dtype, 85, "cuda")])
+        qb = torch.cat([qf[:, :, -1:], randn((2, H, 1, D), dtype, 86, "cuda")])
+        yb = bi.scaled_dot_product_attention(qb, kb, vb, mask="causal")
+        assert np.array_equal(bits(yb[:1, :, -1]), base), (D, V, "batch")
+        # one more key, masked off: same bits
+        k1 = torch.cat([k, randn((1, Hkv, 1, D), dtype, 87, "cuda")], dim=2)
+        v1 = torch.cat([v, randn((1, Hkv, 1, V), dtype, 88, "cuda")], dim=2)
+        keep = torch.ones(1, 1, 1, N + 1, dtype=torch.bool, device="cuda")
+        keep[..., N] = False
+        y1 = bi.scaled_dot_product_attention(qf[:, :, -1:].contiguous(), k1, v1, mask=keep)
+        assert np.array_equal(bits(y1[:, :, -1]), base), (D, V, "masked extra key")
+
+
+def test_head_dims_beyond_the_built_range_raise(bi):
+    q = randn((1, 2, 1, 672), torch.bfloat16, 1, "cuda")
+    with pytest.raises(NotImplementedError):
+        bi.scaled_dot_product_attention(q, q, q)
+    q32 = randn((1, 2, 1, 416), torch.float32, 1, "cuda")
+    with pytest.raises(NotImplementedError):
+        bi.scaled_dot_product_attention(q32, q32, q32)
