@@ -375,8 +375,9 @@ def prompts(cfg, batch, length, device, seed=7):
 
 
 def slot0_bits(logits):
-    """The slot-0 rows of a generate() run, as raw 16-bit patterns (steps, vocab)."""
-    return torch.stack([t[0] for t in logits]).view(torch.int16)
+    """The slot-0 rows of a generate() run, as raw bit patterns (steps, vocab)."""
+    rows = torch.stack([t[0] for t in logits])
+    return rows.view(torch.int32 if rows.element_size() == 4 else torch.int16)
 
 
 def differing(a, b):

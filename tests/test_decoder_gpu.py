@@ -157,3 +157,87 @@ def test_fused_swiglu_is_within_one_ulp_of_torch():
     w = want.float()
     ulp = torch.clamp(w.abs(), min=2.0 ** -126) * 2.0 ** -7
     assert ((a - w).abs() <= ulp).all()
+
+
+def _eager_slot0(model, batch, prompt=21, steps=4):
+    from mlx_batch_invariant_b200 import decoder as dec
+    ids = dec.prompts(model.cfg, batch, prompt, "cuda")
+    logits, _, _ = dec.generate(model, ids, steps)
+    return dec.slot0_bits(logits)
+
+
+def test_stock_decoder_is_batch_variant_somewhere_control():
+    """Negative control for the decoder (the role of the reference's stock-MLX row in
+    bench/bench.py:211-246): stock torch (cuBLAS + SDPA) on this model must give the
+    shared slot-0 prompt different logits at some batch size or dtype -- and the
+    invariant path, on that same model and batch, none."""
+    import mlx_batch_invariant_b200 as bi
+    from mlx_batch_invariant_b200 import decoder as dec
+    found = []
+    for dtype in (torch.bfloat16, torch.float32):
+        m = dec.Decoder(dec.DecoderConfig(**SMALL), max_batch=64, max_len=32, dtype=dtype,
+                        device="cuda")
+        try:
+            base = _eager_slot0(m, 1)
+            variant = [B for B in (8, 33, 64) if any(dec.differing(_eager_slot0(m, B), base))]
+            if variant:
+                found.append((dtype, variant))
+                with bi.batch_invariant_mode(strict=True):
+                    ibase = _eager_slot0(m, 1)
+                    for B in variant:
+                        assert not any(dec.differing(_eager_slot0(m, B), ibase)), (dtype, B)
+        finally:
+            m.close()
+    assert found, "stock torch gave every batch the same slot-0 logits in bf16 and fp32"
+
+
+def test_invariant_logits_are_as_close_to_an_fp32_forward_as_stock():
+    """The invariant bf16 model against a float32 forward of the same weights (stock
+    torch, no TF32), on the prefill and three decode steps fed the fp32 model's greedy
+    tokens: its normwise error max|ours - fp32| / max|fp32| stays within twice stock
+    bf16's and under 5e-2 (the reference's bar for its quantized path,
+    tests/test_invariance.py:585-592, and its bf16 GEMM bar)."""
+    import mlx_batch_invariant_b200 as bi
+    from mlx_batch_invariant_b200 import decoder as dec
+    assert not torch.backends.cuda.matmul.allow_tf32
+    cfg = dec.DecoderConfig(**SMALL)
+    m16 = dec.Decoder(cfg, max_batch=2, max_len=40, device="cuda")
+    m32 = dec.Decoder(cfg, max_batch=2, max_len=40, dtype=torch.float32, device="cuda")
+    try:
+        for l16, l32 in zip(m16.layers, m32.layers):
+            for key in l16:
+                l32[key].copy_(l16[key].float())
+        for name in ("embed", "norm", "head"):
+            getattr(m32, name).copy_(getattr(m16, name).float())
+        ids = dec.prompts(cfg, 2, 37, "cuda")
+
+        def run(model, mode):
+            with (bi.batch_invariant_mode(strict=True) if mode else _null()):
+                out = [model.prefill(ids).double()]
+                for t in toks:
+                    out.append(model.decode(t).double())
+            return torch.stack(out)
+
+        toks = []
+        ref = [m32.prefill(ids).double()]
+        for _ in range(3):
+            toks.append(ref[-1].argmax(dim=-1))
+            ref.append(m32.decode(toks[-1]).double())
+        ref = torch.stack(ref)
+        ours = run(m16, True)
+        stock = run(m16, False)
+        scale = ref.abs().max()
+        e_ours = ((ours - ref).abs().max() / scale).item()
+        e_stock = ((stock - ref).abs().max() / scale).item()
+        assert e_ours <= 2 * e_stock + 1e-6 and e_ours < 5e-2, (e_ours, e_stock)
+    finally:
+        m16.close()
+        m32.close()
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
