@@ -78,6 +78,23 @@ int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb,
             float alpha, float beta, int dtype, void* stream);
 
 /*
+ * float32 bi_gemm on the tensor cores: the same contract as bi_gemm with dtype BI_F32,
+ * run as three tf32 products per K step (tcgen05.mma kind::tf32: a_big*b_big +
+ * a_big*b_small + a_small*b_big, x = big + small exactly, big = x with its low 13
+ * mantissa bits cleared) with fp32 accumulation; one 256 x 256 pair tile and K
+ * order for every M, so rows are batch-invariant.  Within the reference's float32
+ * accuracy bar against float64 (mlx_batch_invariant tests/test_invariance.py:114-127),
+ * not bit-equal to bi_gemm's CUDA-core fp32 route.  No counterpart in the reference
+ * (whose fp32 path is the same bi_gemm kernel).  Needs K % 4 == 0 (and N % 4 == 0 for
+ * a (K, N) b), 16-byte aligned a / b and row strides that are multiples of 4 elements;
+ * else BI_ERR_UNSUPPORTED / BI_ERR_MISALIGNED.
+ */
+int bi_gemm_tf32x3(const void* a, int64_t lda, const void* b, int64_t ldb,
+                   const void* bias, void* out, int64_t ldo,
+                   int64_t M, int64_t N, int64_t K, int b_is_nk,
+                   float alpha, float beta, void* stream);
+
+/*
  * The kernel route and CTA tile bi_gemm uses for (dtype, K, N, layout).  The result
  * never depends on M; this is the library's analogue of the reference's public
  * TILE constant (_gemm.py:27).  Any out-pointer may be null.

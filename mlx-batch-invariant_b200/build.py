@@ -22,7 +22,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "mlx_batch_invariant_b200", "libbi.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["capi.cu", "gemm_tcgen05.cu", "gemm_simt.cu", "sdpa.cu", "harness.cu"]
+SOURCES = ["capi.cu", "gemm_tcgen05.cu", "gemm_tf32x3.cu", "gemm_simt.cu", "sdpa.cu",
+           "harness.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I" + INCLUDE, "-I" + CSRC]

@@ -104,6 +104,11 @@ static int ensure_peer_access(int cur, int peer) {
   return BI_OK;
 }
 
+// Shapes the fp32 tensor-core route takes: TMA needs 16-byte row strides.
+static bool tf32x3_shape_ok(int64_t K, int64_t N, int b_is_nk) {
+  return K > 0 && K % 4 == 0 && (b_is_nk || N % 4 == 0);
+}
+
 static int check_device() {
   const int cc = device_cc_major();
   if (cc < 0) return set_error(BI_ERR_NO_DEVICE, "no CUDA device is current");
@@ -148,6 +153,32 @@ int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb, const void* 
     return launch_gemm_tc(g, s);
   }
   return launch_gemm_simt(g, s);
+}
+
+int bi_gemm_tf32x3(const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
+                   void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int b_is_nk,
+                   float alpha, float beta, void* stream) {
+  g_msg[0] = '\0';
+  if (M < 0 || N < 0 || K < 0) return set_error(BI_ERR_INVALID, "negative dimension");
+  if (M == 0 || N == 0) return BI_OK;
+  if (out == nullptr) return set_error(BI_ERR_INVALID, "out is null");
+  if (K > 0 && (a == nullptr || b == nullptr)) return set_error(BI_ERR_INVALID, "a or b is null");
+  if (lda < K || ldo < N || ldb < (b_is_nk ? K : N)) {
+    return set_error(BI_ERR_INVALID, "leading dimension smaller than the row");
+  }
+  if (!tf32x3_shape_ok(K, N, b_is_nk)) {
+    return set_error(BI_ERR_UNSUPPORTED,
+                     "the tf32x3 route needs K %% 4 == 0 (and N %% 4 == 0 for a (K, N) b)");
+  }
+  if (!aligned16(a) || !aligned16(b) || lda % 4 != 0 || ldb % 4 != 0) {
+    return set_error(BI_ERR_MISALIGNED,
+                     "the tf32x3 route needs 16-byte aligned a/b and row strides that are "
+                     "multiples of 4 elements");
+  }
+  int st = check_device();
+  if (st) return st;
+  GemmArgs g{a, lda, b, ldb, bias, out, ldo, M, N, K, b_is_nk ? 1 : 0, alpha, beta, BI_F32};
+  return launch_gemm_tf32x3(g, static_cast<cudaStream_t>(stream));
 }
 
 int bi_gemm_route(int dtype, int64_t K, int64_t N, int b_is_nk, int* route, int* bm, int* bn,
@@ -566,8 +597,10 @@ int bi_device_error(int clear) {
   unsigned w = read_error_gemm_tc(clear != 0);
   const unsigned s = read_error_sdpa(clear != 0);
   const unsigned h = read_error_harness(clear != 0);
+  const unsigned t = read_error_tf32x3(clear != 0);
   if (w == 0 && s != 0) w = s | (1u << 16);  // sdpa sites are tagged in bit 16
   if (w == 0 && h != 0) w = h | (1u << 17);  // decoder-harness sites in bit 17
+  if (w == 0 && t != 0) w = t | (1u << 18);  // fp32 tensor-core GEMM sites in bit 18
   return static_cast<int>(w);
 }
 

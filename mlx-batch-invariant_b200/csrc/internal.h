@@ -112,12 +112,14 @@ int launch_gather_unpack(const GatherArgs& x, void* out_base, int64_t ldo, int64
 int launch_peer_barrier(const GatherArgs& x, cudaStream_t stream);
 int static_flag_block(int device, void** out);
 int launch_gemm_simt(const GemmArgs& g, cudaStream_t stream);
+int launch_gemm_tf32x3(const GemmArgs& g, cudaStream_t stream);
 int launch_sdpa(const SdpaArgs& s, cudaStream_t stream);
 
 // Device error words, one per translation unit; read and optionally clear.
 unsigned read_error_gemm_tc(bool clear);
 unsigned read_error_sdpa(bool clear);
 unsigned read_error_harness(bool clear);
+unsigned read_error_tf32x3(bool clear);
 
 // Per-thread message for bi_last_error().
 int set_error(int status, const char* fmt, ...);

@@ -24,6 +24,7 @@ from . import _ops  # noqa: F401  (registers mlx_bi::gemm and mlx_bi::sdpa)
 from ._attention import _mask_args, _sdpa, scaled_dot_product_attention
 from ._attention import head_dims_built
 from ._gemm import QUANT_BITS, SIMT_TILE, TILE, addmm, linear, matmul, quantized_linear, tile_for
+from ._gemm import float32_gemm, get_float32_gemm, set_float32_gemm
 
 __all__ = [
     "quantized_linear",
@@ -37,6 +38,9 @@ __all__ = [
     "TILE",
     "SIMT_TILE",
     "tile_for",
+    "set_float32_gemm",
+    "get_float32_gemm",
+    "float32_gemm",
     "__version__",
 ]
 

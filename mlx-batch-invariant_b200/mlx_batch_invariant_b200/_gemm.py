@@ -8,9 +8,46 @@ bias is added to the fp32 accumulator before the single rounding, so a row's bit
 not depend on the other rows computed with it.
 """
 
+import contextlib
+
 import torch
 
 from . import _lib
+
+# How float32 GEMMs run: "exact" -- the CUDA-core route, the reference's fp32 K order
+# bit for bit -- or "tf32x3" -- the tensor-core route, three tf32 products per K step
+# (within the reference's float32 accuracy bar, not bit-equal to "exact").  Either is
+# batch-invariant; pick one per process or model run, not per call.
+_FLOAT32_GEMM = "exact"
+_FLOAT32_GEMMS = ("exact", "tf32x3")
+
+
+def set_float32_gemm(mode):
+    """Selects the float32 GEMM route: "exact" (default) or "tf32x3"."""
+    global _FLOAT32_GEMM
+    if mode not in _FLOAT32_GEMMS:
+        raise ValueError("float32 GEMM route must be one of %s, got %r" % (_FLOAT32_GEMMS, mode))
+    _FLOAT32_GEMM = mode
+
+
+def get_float32_gemm():
+    return _FLOAT32_GEMM
+
+
+@contextlib.contextmanager
+def float32_gemm(mode):
+    """Runs the block with the float32 GEMM route `mode`, restoring the previous one."""
+    prev = _FLOAT32_GEMM
+    set_float32_gemm(mode)
+    try:
+        yield
+    finally:
+        set_float32_gemm(prev)
+
+
+def _tf32x3_takes(dtype, K, N, b_is_nk):
+    return (dtype == torch.float32 and _FLOAT32_GEMM == "tf32x3" and K > 0 and K % 4 == 0
+            and (b_is_nk or N % 4 == 0))
 
 # The tensor-core tile used for float16 / bfloat16, fixed for every shape and every M
 # (cf. the reference's TILE, _gemm.py:27): BM rows per CTA, a pair of CTAs
@@ -22,7 +59,10 @@ SIMT_TILE = dict(BM=128, BN=128, BK=8)
 
 
 def tile_for(dtype, K, N, b_is_nk=True):
-    """The route and tile bi_gemm takes for (dtype, K, N, layout); independent of M."""
+    """The route and tile bi_gemm takes for (dtype, K, N, layout) under the current
+    float32 setting; independent of M."""
+    if _tf32x3_takes(dtype, K, N, b_is_nk):
+        return dict(route="tf32x3", BM=128, BN=256, BK=32)
     r, bm, bn, bk = _lib.route(dtype, K, N, b_is_nk)
     return dict(route="tcgen05" if r == _lib.ROUTE_TCGEN05 else "simt", BM=bm, BN=bn, BK=bk)
 
@@ -99,12 +139,20 @@ def _gemm_eager(a, b, bias, transpose_b, alpha=1.0, beta=1.0, out=None):
         raise ValueError("out must be a contiguous (%d, %d) %s tensor" % (M, N, a.dtype))
     if M and N:
         with torch.cuda.device(dev):
-            st = _lib.lib().bi_gemm(
-                a2.data_ptr(), K, b2.data_ptr(), b2.shape[1],
-                bias2.data_ptr() if bias2 is not None else None,
-                out.data_ptr(), N, M, N, K, 1 if transpose_b else 0, float(alpha), float(beta),
-                code, _lib.stream_handle(dev))
-        _lib.check(st, "bi_gemm")
+            if _tf32x3_takes(a.dtype, K, N, transpose_b):
+                st = _lib.lib().bi_gemm_tf32x3(
+                    a2.data_ptr(), K, b2.data_ptr(), b2.shape[1],
+                    bias2.data_ptr() if bias2 is not None else None,
+                    out.data_ptr(), N, M, N, K, 1 if transpose_b else 0, float(alpha),
+                    float(beta), _lib.stream_handle(dev))
+                _lib.check(st, "bi_gemm_tf32x3")
+            else:
+                st = _lib.lib().bi_gemm(
+                    a2.data_ptr(), K, b2.data_ptr(), b2.shape[1],
+                    bias2.data_ptr() if bias2 is not None else None,
+                    out.data_ptr(), N, M, N, K, 1 if transpose_b else 0, float(alpha),
+                    float(beta), code, _lib.stream_handle(dev))
+                _lib.check(st, "bi_gemm")
     return out.reshape(*lead, N)
 
 

@@ -42,6 +42,9 @@ def _bind(lib):
     lib.bi_gemm.restype = ctypes.c_int
     lib.bi_gemm.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int,
                             ctypes.c_float, ctypes.c_float, ctypes.c_int, _vp]
+    lib.bi_gemm_tf32x3.restype = ctypes.c_int
+    lib.bi_gemm_tf32x3.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64,
+                                   ctypes.c_int, ctypes.c_float, ctypes.c_float, _vp]
     lib.bi_gemm_route.restype = ctypes.c_int
     lib.bi_gemm_route.argtypes = [ctypes.c_int, _i64, _i64, ctypes.c_int,
                                   ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
