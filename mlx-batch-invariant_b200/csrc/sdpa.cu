@@ -790,27 +790,16 @@ constexpr int BOX_D = 64;            // columns per TMA box (128-byte rows)
 template <int D>
 constexpr int default_stages() { return D == 128 ? 1 : 2; }
 
-//
-// A cluster of C CTAs can share one (batch, query row, 4 heads) row: CTA c of the
-// cluster owns partials [c * 32 / C, (c + 1) * 32 / C) -- their keys, their softmax
-// states -- and the combine reads every partial's state through distributed shared
-// memory in the fixed order p = 0..31, each CTA producing D / C of the output columns.
-// The fold and the combine are the same operations in the same order for every C; C
-// only spreads a row's partials over more SMs (small grids: a head shard on 4 or 8
-// GPUs).
-template <int D, int STAGES_, int C = 1>
+template <int D, int STAGES_>
 struct Plan {
   static constexpr int BOXES = D / BOX_D;
-  static constexpr int KEYS_L = KEYS / C;                 // keys of this CTA per stage
-  static constexpr int PPC = PARTIALS / C;                // partials per CTA
-  static constexpr int TSB = KEYS_L * D * 2;              // one tensor's stage bytes
+  static constexpr int TSB = KEYS * D * 2;               // one tensor's stage bytes
   static constexpr int STAGES = STAGES_;
-  static constexpr int COMB = 4 * PPC * D * 4 + 2 * 4 * PPC * 4 + 2 * 4 * PARTIALS * 4 + 64;
+  static constexpr int COMB = 4 * PARTIALS * D * 4 + 2 * 4 * PARTIALS * 4 + 64;
   static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
   static constexpr int SMEM = 1024 + REGION + STAGES * 8 + 64;
   static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
   static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
-  static_assert(C == 1 || C == 2 || C == 4, "clusters of 1, 2 or 4 CTAs");
 };
 
 template <typename T>
@@ -842,21 +831,11 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
 }
 
 // Shared-memory address of the 16-byte chunk holding columns [d, d + 8) of stage row
-// `row`: one TMA region per 64 columns (ROWS rows of 128 B), chunks swizzled by row % 8.
-template <int ROWS>
+// `row`: one TMA box per 64 columns (KEYS rows of 128 B), chunks swizzled by row % 8.
 __device__ __forceinline__ uint32_t kv_addr(uint32_t base, int row, int d) {
   const int box = d >> 6;
   const int c = (d & 63) >> 3;
-  return base + box * (ROWS * 128) + row * 128 + ((c ^ (row & 7)) << 4);
-}
-
-// A float in CTA `cta`'s shared memory at the offset of `local` (distributed shared
-// memory of the cluster).
-__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t cta) {
-  const uint32_t a = map_to_cta(smem_u32(local), cta);
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
+  return base + box * (KEYS * 128) + row * 128 + ((c ^ (row & 7)) << 4);
 }
 
 // Two fp32 values -> one register of two 16-bit T (round to nearest even), and what
@@ -884,15 +863,12 @@ __device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
   return pack_rn<T>(lo, hi, a, b);
 }
 
-template <typename T, int D, int GH, int S, int C>
-__global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
+template <typename T, int D, int GH, int S>
+__global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
     sdpa_mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const Params p) {
-  using PL = Plan<D, S, C>;
-  static_assert(C == 1 || GH == 4, "clusters split the partials of four heads");
-  constexpr int NW = 2 * GH / C;     // warps: 16 MMA rows each
-  constexpr int KEYS_L = PL::KEYS_L;
-  constexpr int PPC = PL::PPC;
+  using PL = Plan<D, S>;
+  constexpr int NW = 2 * GH;         // warps: 16 MMA rows each
   constexpr int NT = 32 * NW;
   constexpr int NPW = 16 / GH;       // partials per warp
   constexpr int KG = NPW / 4;        // 16-key MMA steps per warp per stage
@@ -919,9 +895,7 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
   const int q4 = lane & 3;
 
   const int groups = p.H / GH;
-  int idx = blockIdx.x / C;
-  const int crank = C > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int p0 = crank * PPC;  // first partial of this CTA
+  int idx = blockIdx.x;
   const int s = idx % p.qL;
   idx /= p.qL;
   const int hg = idx % groups;
@@ -936,11 +910,10 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
   }
   const int nblocks = static_cast<int>((kmax + KEYS - 1) / KEYS);
 
-  // This thread's two rows: same head, partials part[0] and part[1] (local lpart).
+  // This thread's two rows: same head, partials part[0] and part[1].
   const int head = gq % GH;
   int pp[2] = {gq / GH, (gq + 8) / GH};
-  int lpart[2] = {warp * NPW + pp[0], warp * NPW + pp[1]};
-  int part[2] = {p0 + lpart[0], p0 + lpart[1]};
+  int part[2] = {warp * NPW + pp[0], warp * NPW + pp[1]};
 
   const T* Q = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.qs0 +
                static_cast<int64_t>(h0 + head) * p.qs1 + static_cast<int64_t>(s) * p.qs2;
@@ -977,21 +950,10 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
     mbar_arrive_expect_tx(&full[st], 2 * TSB);
 #pragma unroll
     for (int bx = 0; bx < PL::BOXES; ++bx) {
-      if constexpr (C == 1) {
-        tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh,
-                    b);
-        tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh,
-                    b);
-      } else {
-        // this CTA's partials: PPC consecutive keys out of every 32
-#pragma unroll
-        for (int j = 0; j < R; ++j) {
-          const int key = blk * KEYS + j * PARTIALS + p0;
-          const int off = bx * KEYS_L * 128 + j * PPC * 128;
-          tma_load_4d(sK + st * TSB + off, &tk, &full[st], bx * BOX_D, key, kvh, b);
-          tma_load_4d(sV + st * TSB + off, &tv, &full[st], bx * BOX_D, key, kvh, b);
-        }
-      }
+      tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh,
+                  b);
+      tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh,
+                  b);
     }
   };
 
@@ -1029,20 +991,19 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
     const int64_t key0 = static_cast<int64_t>(t) * KEYS;
 #pragma unroll
     for (int g = 0; g < KG; ++g) {
-      const int lbase = warp * NPW + 4 * g;  // first partial of this MMA step (local)
-      const int pbase = p0 + lbase;          // ... and its index among the 32
+      const int pbase = warp * NPW + 4 * g;  // first partial of this MMA step
       // ---- scores: 16 rows x 16 key positions (position = 4 * j + partial % 4)
       float sc[2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
         const int pos = 8 * nt + (lane & 7);
-        const int krow = PPC * (pos >> 2) + lbase + (pos & 3);
+        const int krow = 32 * (pos >> 2) + pbase + (pos & 3);
         const int mi = lane >> 3;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; kk += 2) {
           uint32_t bf[4];
-          ldsm_x4(bf, kv_addr<KEYS_L>(kbase, krow, 16 * (kk + (mi >> 1)) + 8 * (mi & 1)));
+          ldsm_x4(bf, kv_addr(kbase, krow, 16 * (kk + (mi >> 1)) + 8 * (mi & 1)));
           mma16816<T>(sc[nt], qa[kk][0], qa[kk][0], qa[kk][1], qa[kk][1], bf[0], bf[1]);
           mma16816<T>(sc[nt], qa[kk + 1][0], qa[kk + 1][0], qa[kk + 1][1], qa[kk + 1][1], bf[2],
                       bf[3]);
@@ -1117,11 +1078,11 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
       // ---- o += P V over this step's 16 keys (P = P_hi + P_lo)
       const int mi = lane >> 3;
       const int vpos = 8 * (mi & 1) + (lane & 7);
-      const int vrow = PPC * (vpos >> 2) + lbase + (vpos & 3);
+      const int vrow = 32 * (vpos >> 2) + pbase + (vpos & 3);
 #pragma unroll
       for (int nd = 0; nd < NTD; nd += 2) {
         uint32_t bv[4];
-        ldsm_x4_t(bv, kv_addr<KEYS_L>(vbase, vrow, 8 * (nd + (mi >> 1))));
+        ldsm_x4_t(bv, kv_addr(vbase, vrow, 8 * (nd + (mi >> 1))));
         mma16816<T>(o[nd], phi[0], phi[1], phi[2], phi[3], bv[0], bv[1]);
         mma16816<T>(o[nd], plo[0], plo[1], plo[2], plo[3], bv[0], bv[1]);
         mma16816<T>(o[nd + 1], phi[0], phi[1], phi[2], phi[3], bv[2], bv[3]);
@@ -1143,94 +1104,52 @@ __global__ void __launch_bounds__(64 * GH / C, (Plan<D, S, C>::CTAS_PER_SM))
       }
     }
   }
-  const bool any_aborted = __syncthreads_or(aborted);
-  if (any_aborted) {
+  if (__syncthreads_or(aborted)) {
     if (tid == 0) {
       const int issued = *issued_count;
       for (int blk = issued - STAGES < 0 ? 0 : issued - STAGES; blk < issued; ++blk) {
         mbar_wait(&full[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
       }
     }
-    // a cluster's CTAs still meet at both cluster barriers below
-    if constexpr (C == 1) return;
+    return;
   }
   __syncthreads();  // every stage consumed and no copy in flight: the ring is free
 
   // ---- combine the 32 partials of every head, p = 0..31
-  float* comb_o = reinterpret_cast<float*>(smem);               // [GH][PPC][D]
-  float* comb_m = comb_o + GH * PPC * D;                        // [GH][PPC]
-  float* comb_l = comb_m + GH * PPC;                            // [GH][PPC]
+  float* comb_o = reinterpret_cast<float*>(smem);               // [GH][32][D]
+  float* comb_m = comb_o + GH * PARTIALS * D;                   // [GH][32]
+  float* comb_l = comb_m + GH * PARTIALS;                       // [GH][32]
 #pragma unroll
   for (int ri = 0; ri < 2; ++ri) {
-    float* row = comb_o + (head * PPC + lpart[ri]) * D;
+    float* row = comb_o + (head * PARTIALS + part[ri]) * D;
 #pragma unroll
     for (int nd = 0; nd < NTD; ++nd) {
       *reinterpret_cast<float2*>(row + 8 * nd + 2 * q4) = make_float2(o[nd][2 * ri], o[nd][2 * ri + 1]);
     }
     if (q4 == 0) {
-      comb_m[head * PPC + lpart[ri]] = m[ri];
-      comb_l[head * PPC + lpart[ri]] = l[ri];
+      comb_m[head * PARTIALS + part[ri]] = m[ri];
+      comb_l[head * PARTIALS + part[ri]] = l[ri];
     }
   }
+  float* comb_s = comb_l + GH * PARTIALS;                       // [GH] denominators
+  __syncthreads();
+  if (warp < GH) {
+    const float ls = combine_weights(comb_m + warp * PARTIALS, comb_l + warp * PARTIALS, lane);
+    if (lane == 0) comb_s[warp] = ls;  // comb_m now holds the f_q of each head
+  }
+  __syncthreads();
   T* O = static_cast<T*>(p.out);
-  if constexpr (C == 1) {
-    float* comb_s = comb_l + GH * PARTIALS;                     // [GH] denominators
-    __syncthreads();
-    if (warp < GH) {
-      const float ls = combine_weights(comb_m + warp * PARTIALS, comb_l + warp * PARTIALS, lane);
-      if (lane == 0) comb_s[warp] = ls;  // comb_m now holds the f_q of each head
-    }
-    __syncthreads();
-    for (int jj = tid; jj < GH * D; jj += NT) {
-      const int hh = jj / D;
-      const int j = jj - hh * D;
-      const float* fq = comb_m + hh * PARTIALS;
-      const float lsum = comb_s[hh];
-      float acc = 0.f;
+  for (int jj = tid; jj < GH * D; jj += NT) {
+    const int hh = jj / D;
+    const int j = jj - hh * D;
+    const float* fq = comb_m + hh * PARTIALS;
+    const float lsum = comb_s[hh];
+    float acc = 0.f;
 #pragma unroll 8
-      for (int q = 0; q < PARTIALS; ++q) acc = __fmaf_rn(comb_o[(hh * PARTIALS + q) * D + j], fq[q], acc);
-      const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
-      O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + hh) * p.os1 +
-        static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
-    }
-  } else {
-    // every CTA's partial states written: gather the 32 (m, l) of each head in partial
-    // order (partial q lives in CTA q / PPC), form the combine weights, then this CTA's
-    // D / C output columns from every CTA's numerators
-    float* gm = comb_l + GH * PPC;                              // [GH][32]
-    float* gl = gm + GH * PARTIALS;                             // [GH][32]
-    float* gs = gl + GH * PARTIALS;                             // [GH]
-    cluster_sync();
-    if (!any_aborted) {
-      for (int hh = warp; hh < GH; hh += NW) {
-        const uint32_t src = static_cast<uint32_t>(lane / PPC);
-        const int li = hh * PPC + lane % PPC;
-        gm[hh * PARTIALS + lane] = ld_cluster_f32(comb_m + li, src);
-        gl[hh * PARTIALS + lane] = ld_cluster_f32(comb_l + li, src);
-        __syncwarp();
-        const float ls = combine_weights(gm + hh * PARTIALS, gl + hh * PARTIALS, lane);
-        if (lane == 0) gs[hh] = ls;  // gm now holds the f_q of head hh
-      }
-      __syncthreads();
-      constexpr int DC = D / C;
-      for (int jj = tid; jj < GH * DC; jj += NT) {
-        const int hh = jj / DC;
-        const int j = crank * DC + (jj - hh * DC);
-        const float* fq = gm + hh * PARTIALS;
-        const float lsum = gs[hh];
-        float acc = 0.f;
-#pragma unroll 8
-        for (int q = 0; q < PARTIALS; ++q) {
-          const float oq = ld_cluster_f32(comb_o + (hh * PPC + q % PPC) * D + j,
-                                          static_cast<uint32_t>(q / PPC));
-          acc = __fmaf_rn(oq, fq[q], acc);
-        }
-        const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
-        O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + hh) * p.os1 +
-          static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
-      }
-    }
-    cluster_sync();  // no CTA leaves while the others read its shared memory
+    for (int q = 0; q < PARTIALS; ++q) acc = __fmaf_rn(comb_o[(hh * PARTIALS + q) * D + j], fq[q], acc);
+    const float res = lsum == 0.f ? acc : __fdiv_rn(acc, lsum);
+    O[static_cast<int64_t>(b) * p.os0 + static_cast<int64_t>(h0 + hh) * p.os1 +
+      static_cast<int64_t>(s) * p.os2 + j] = from_f32<T>(res);
   }
 }
 
@@ -1331,8 +1250,7 @@ namespace tcr {
 // K or V as a 4-D TMA map (D, N, Hkv, B): rows of a head are contiguous; a dimension
 // of extent 1 gets a compact stride, any other must be a positive multiple of 16 B.
 template <int D>
-static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], const SdpaArgs& a,
-                  uint32_t box_rows) {
+static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], const SdpaArgs& a) {
   const uint64_t rows = a.N > 0 ? static_cast<uint64_t>(a.N) : 1;
   uint64_t dims[4] = {static_cast<uint64_t>(D), rows, static_cast<uint64_t>(a.Hkv),
                       static_cast<uint64_t>(a.B)};
@@ -1346,43 +1264,25 @@ static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], co
                                           "multiples of 8 elements");
     }
   }
-  uint32_t box[4] = {BOX_D, box_rows, 1, 1};
+  uint32_t box[4] = {BOX_D, KEYS, 1, 1};
   return encode_tiled16(map, base, 4, dims, strides, box, a.dtype);
 }
 
-template <typename T, int D, int GH, int S = default_stages<D>(), int C = 1>
+template <typename T, int D, int GH, int S = default_stages<D>()>
 static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  using PL = Plan<D, S, C>;
+  using PL = Plan<D, S>;
   CUtensorMap tk, tv;
-  const uint32_t box_rows = C == 1 ? KEYS : PL::PPC;
-  int st = kv_map<D>(&tk, a.k, a.ks, a, box_rows);
+  int st = kv_map<D>(&tk, a.k, a.ks, a);
   if (st) return st;
-  st = kv_map<D>(&tv, a.v, a.vs, a, box_rows);
+  st = kv_map<D>(&tv, a.v, a.vs, a);
   if (st) return st;
-  auto kern = sdpa_mma_kernel<T, D, GH, S, C>;
+  auto kern = sdpa_mma_kernel<T, D, GH, S>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        PL::SMEM);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa tc)");
-  const int64_t blocks = a.B * (a.H / GH) * a.qL * C;
+  const int64_t blocks = a.B * (a.H / GH) * a.qL;
   if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "too many attention rows");
-  if constexpr (C == 1) {
-    kern<<<static_cast<unsigned>(blocks), 64 * GH, PL::SMEM, stream>>>(tk, tv, p);
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
-    cfg.blockDim = dim3(64 * GH / C, 1, 1);
-    cfg.dynamicSmemBytes = PL::SMEM;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = C;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
-    if (e != cudaSuccess) return cuda_status(e, "sdpa tc cluster launch");
-  }
+  kern<<<static_cast<unsigned>(blocks), 64 * GH, PL::SMEM, stream>>>(tk, tv, p);
   return cuda_status(cudaGetLastError(), "sdpa tc launch");
 }
 
@@ -1391,7 +1291,7 @@ static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
 // columns, whatever the other rows hold, and the ring only stages keys, so both decide
 // which CTA computes a row and how its keys arrive -- never the row's bits.
 struct TcPlan {
-  int gh, stages, cluster;
+  int gh, stages;
 };
 
 // Four heads per CTA always (2 or 1 repeat the key-side MMAs per head: measured 1.5-4x
@@ -1400,7 +1300,7 @@ struct TcPlan {
 // B = 64, H = 8, Hkv = 2 -- otherwise two CTAs per SM cover each other's latency.
 static TcPlan tc_plan(const SdpaArgs& a, int sms) {
   const int64_t ctas = a.B * (a.H / 4) * a.qL;
-  return TcPlan{4, ctas <= sms ? 3 : 0, 1};
+  return TcPlan{4, ctas <= sms ? 3 : 0};
 }
 
 template <typename T, int D>
@@ -1408,8 +1308,6 @@ static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   const TcPlan pl = tc_plan(a, device_sm_count());
   const bool deep = pl.stages > default_stages<D>();
   (void)pl.gh;  // the kernel also builds for 1 or 2 heads per CTA; 4 is the one routed
-  if (pl.cluster == 4) return launch_gh<T, D, 4, 3, 4>(a, p, stream);
-  if (pl.cluster == 2) return launch_gh<T, D, 4, 3, 2>(a, p, stream);
   return deep ? launch_gh<T, D, 4, 3>(a, p, stream) : launch_gh<T, D, 4>(a, p, stream);
 }
 
