@@ -81,8 +81,9 @@ int bi_gemm(const void* a, int64_t lda, const void* b, int64_t ldb,
  * float32 bi_gemm on the tensor cores: the same contract as bi_gemm with dtype BI_F32,
  * run as three tf32 products per K step (tcgen05.mma kind::tf32: a_big*b_big +
  * a_big*b_small + a_small*b_big, x = big + small exactly, big = x with its low 13
- * mantissa bits cleared) with fp32 accumulation; one 256 x 256 pair tile and K
- * order for every M, so rows are batch-invariant.  Within the reference's float32
+ * mantissa bits cleared) with fp32 accumulation of each 256-deep K chunk on the
+ * tensor cores and the chunk sums added in K order in fp32 (round to nearest); one
+ * 256 x 256 pair tile and K order for every M, so rows are batch-invariant.  Within the reference's float32
  * accuracy bar against float64 (mlx_batch_invariant tests/test_invariance.py:114-127),
  * not bit-equal to bi_gemm's CUDA-core fp32 route.  No counterpart in the reference
  * (whose fp32 path is the same bi_gemm kernel).  Needs K % 4 == 0 (and N % 4 == 0 for

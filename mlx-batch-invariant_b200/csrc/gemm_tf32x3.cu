@@ -7,9 +7,12 @@
 // at most 2^-10 |x|).  Per K=8 step the pair accumulates, in this order,
 //     a_big * b_big,  a_big * b_small,  a_small * b_big
 // and drops a_small * b_small (about 2^-20 of a product).  The tensor core keeps the
-// top 11 significant bits of small, so each product is within about 2^-19 of
-// a * b; the fp32 sum over K runs on the accumulator.  The error against float64 stays
-// within the reference's float32 bar (the GPU tests check <= 5e-6 normwise).
+// top 11 significant bits of small, so each product is within about 2^-19 of a * b.
+// The tensor core's fp32 accumulator drifts by a fraction of an ulp on every MMA
+// (measured: error growing linearly in K, 2.2e-4 normwise at K = 28672 when one
+// accumulator takes all of K), so K is summed in chunks of 256 in TMEM and the
+// epilogue adds the chunk sums in K order in fp32 with round to nearest, keeping the
+// running sum in the output; the GPU tests hold it to 5e-6 normwise against float64.
 //
 // Invariance: as in gemm_tc_kernel -- one pair owns an output element's whole K
 // reduction, the tile (256 x 256), K block (32) and instruction sequence are fixed,
@@ -21,7 +24,8 @@
 //               32-deep K block, completing on this CTA's own full barrier.
 //   warp 1      TMEM allocator and, in the leader, the UMMA issuer (3 x 4 UMMAs per
 //               K block, after both CTAs' converters have signalled the stage).
-//   warps 2..5  epilogue: tcgen05.ld, alpha / beta / bias in fp32, fp32 stores.
+//   warps 2..5  epilogue: tcgen05.ld of each 256-deep K chunk, added to the running
+//               sum in the output; after the last, alpha / beta / bias in fp32.
 //   warps 6..9  converters: rewrite the stage's A and B in place as big and write
 //               small beside them, fence to the async proxy, arrive on the leader.
 // Every mbarrier wait is bounded; a wait that gives up records the device error word.
@@ -40,6 +44,10 @@ constexpr int BK = 32;           // 32 fp32 = one 128-byte swizzle row
 constexpr int UMMA_K = 8;        // kind::tf32: 8 elements (32 bytes) per step
 constexpr int STAGES = 3;
 constexpr int ACC_BUFS = 2;
+// K blocks summed in one TMEM accumulator before the epilogue adds the chunk into the
+// running fp32 sum (round to nearest): the tensor core's fp32 accumulation drifts by a
+// fraction of an ulp per MMA, so its error grows with the MMAs per chunk, not with K.
+constexpr int KB_PER_CHUNK = 8;  // 256 of K
 constexpr int TMEM_COLS = ACC_BUFS * BN;  // 512
 constexpr int OP_BYTES = BM * BK * 4;     // 16 KiB: one operand tile of one CTA
 constexpr int STAGE_BYTES = 4 * OP_BYTES; // A, B (rewritten as big), A small, B small
@@ -242,8 +250,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int it = 0;
-      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs, ++it) {
+      int it = 0;  // chunks issued (each fills one accumulator buffer)
+      for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
+       for (int kc = 0; kc < num_kb && ok; kc += KB_PER_CHUNK, ++it) {
         const int buf = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[buf], acc_phase ^ 1u, abort_flag)) {
@@ -252,7 +261,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kc_end = min(kc + KB_PER_CHUNK, num_kb);
+        for (int kb = kc; kb < kc_end; ++kb) {
           if (!mbar_wait_acq_cluster(&conv[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -264,8 +274,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // K-major, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart; the
-            // K=8 step moves 32 bytes along the row.  MN-major B: 32-column slabs 4 KiB
-            // apart (LBO), 8-k-row groups 1024 B apart; the K=8 step moves 1024 B.
+            // K=8 step moves 32 bytes along the row.  MN-major B (32-bit operands take
+            // only the 128-byte swizzle with 32-byte atoms, layout type 1): 32-column
+            // slabs 4 KiB apart (LBO), 4-k-row groups 512 B apart (SBO); the K=8 step
+            // moves 8 k-rows, 1024 B.
             const uint32_t ko = k * UMMA_K * 4;
             const uint64_t ab = umma_smem_desc(a_big + ko, 16, 1024, 2);
             const uint64_t as = umma_smem_desc(a_small + ko, 16, 1024, 2);
@@ -274,10 +286,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
               bb = umma_smem_desc(b_big + ko, 16, 1024, 2);
               bs = umma_smem_desc(b_small + ko, 16, 1024, 2);
             } else {
-              bb = umma_smem_desc(b_big + k * UMMA_K * 128, 32 * BK * 4, 1024, 2);
-              bs = umma_smem_desc(b_small + k * UMMA_K * 128, 32 * BK * 4, 1024, 2);
+              bb = umma_smem_desc(b_big + k * UMMA_K * 128, 32 * BK * 4, 512, 1);
+              bs = umma_smem_desc(b_small + k * UMMA_K * 128, 32 * BK * 4, 512, 1);
             }
-            umma_tf32_pair(d_tmem, ab, bb, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_tf32_pair(d_tmem, ab, bb, idesc, ((kb - kc) | k) != 0 ? 1u : 0u);
             umma_tf32_pair(d_tmem, ab, bs, idesc, 1u);
             umma_tf32_pair(d_tmem, as, bb, idesc, 1u);
           }
@@ -289,6 +301,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         if (!ok) break;
         umma_commit_pair(&tfull[buf], PAIR_MASK);
+       }
       }
       if (!ok) {
         *abort_flag = 1;
@@ -348,68 +361,107 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const bool vec_ok = (p.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
     const uint32_t tempty_leader0 = map_to_cta(smem_u32(&tempty[0]), 0);
     uint8_t* stg = epi_stage + (warp - 2) * EPI_STAGE_BYTES;
-    int it = 0;
-    for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++it) {
+    int it = 0;  // chunks consumed
+    bool ok = true;
+    for (int tile = pair; tile < p.num_tiles && ok; tile += num_pairs) {
       int tm, tn;
       tile_coords(tile, p, tm, tn);
-      const int buf = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
-      bool ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) {
-        if (lane == 0) {
-          *abort_flag = 1;
-          record_error(&g_error_word, (kSiteEpilogue << 8) | kErrReasonTimeout);
-        }
-        break;
-      }
-      tc_fence_after();
       const int64_t row_base =
           static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + quarter * 32;
       const int64_t row = row_base + lane;
+      for (int kc = 0; kc < num_kb; kc += KB_PER_CHUNK, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        ok = mbar_wait(&tfull[buf], acc_phase, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) {
+          if (lane == 0) {
+            *abort_flag = 1;
+            record_error(&g_error_word, (kSiteEpilogue << 8) | kErrReasonTimeout);
+          }
+          break;
+        }
+        tc_fence_after();
+        // Chunk sums enter the output in K order: the first is stored as is, each later
+        // one is added (fp32, round to nearest) to the running sum the same thread
+        // stored before, and the last one's total takes alpha / beta / bias and the
+        // final store.  The thread that owns an element is the same in every chunk.
+        const bool first = kc == 0;
+        const bool last = kc + KB_PER_CHUNK >= num_kb;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += EPI_COLS) {
-        const int col0 = tn * BN + c;
-        uint32_t r[32];
+        for (int c = 0; c < BN; c += EPI_COLS) {
+          const int col0 = tn * BN + c;
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32x32b_x32(tmem_base + buf * BN + c + (static_cast<uint32_t>(quarter * 32) << 16),
+                             r);
+          tmem_ld_wait();
+          if (col0 >= p.N) continue;
+          if (vec_ok && col0 + 32 <= p.N) {
+            // stage the warp's 32 x 32 chunk block (row `lane`, 16-byte piece u at
+            // u ^ (lane & 7)); then lane (lr, u) handles 4 columns of row lr, 4 rows at a
+            // time, 128 contiguous bytes per row
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                  make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2], r[4 * u + 3]);
+            }
+            __syncwarp();
+            const int u = lane & 7;
+            const int cc = col0 + u * 4;
+            float4 prev[8];
+            if (!first) {
+#pragma unroll
+              for (int rr = 0; rr < 8; ++rr) {
+                const int64_t grow = row_base + rr * 4 + (lane >> 3);
+                prev[rr] = grow < p.M ? *reinterpret_cast<const float4*>(out + grow * p.ldo + cc)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) {
+              const int lr = rr * 4 + (lane >> 3);
+              const int64_t grow = row_base + lr;
+              float4 val =
+                  *reinterpret_cast<const float4*>(stg + lr * 128 + ((u ^ (lr & 7)) << 4));
+              if (!first) {
+                val.x = __fadd_rn(prev[rr].x, val.x);
+                val.y = __fadd_rn(prev[rr].y, val.y);
+                val.z = __fadd_rn(prev[rr].z, val.z);
+                val.w = __fadd_rn(prev[rr].w, val.w);
+              }
+              if (last) {
+                const float b0 = p.has_bias ? bias[cc] : 0.f;
+                const float b1 = p.has_bias ? bias[cc + 1] : 0.f;
+                const float b2 = p.has_bias ? bias[cc + 2] : 0.f;
+                const float b3 = p.has_bias ? bias[cc + 3] : 0.f;
+                val.x = gemm_epilogue<float>(val.x, p.has_bias, p.alpha, p.beta, b0);
+                val.y = gemm_epilogue<float>(val.y, p.has_bias, p.alpha, p.beta, b1);
+                val.z = gemm_epilogue<float>(val.z, p.has_bias, p.alpha, p.beta, b2);
+                val.w = gemm_epilogue<float>(val.w, p.has_bias, p.alpha, p.beta, b3);
+              }
+              if (grow < p.M) *reinterpret_cast<float4*>(out + grow * p.ldo + cc) = val;
+            }
+            __syncwarp();
+          } else if (row < p.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (col0 + j < p.N) {
+                float v = __uint_as_float(r[j]);
+                if (!first) v = __fadd_rn(out[row * p.ldo + col0 + j], v);
+                if (last) {
+                  v = gemm_epilogue<float>(v, p.has_bias, p.alpha, p.beta,
+                                           p.has_bias ? bias[col0 + j] : 0.f);
+                }
+                out[row * p.ldo + col0 + j] = v;
+              }
+            }
+          }
+        }
+        tc_fence_before();
         __syncwarp();
-        tmem_ld_32x32b_x32(tmem_base + buf * BN + c + (static_cast<uint32_t>(quarter * 32) << 16), r);
-        tmem_ld_wait();
-        if (col0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float bj = (p.has_bias && col0 + j < p.N) ? bias[col0 + j] : 0.f;
-          v[j] = gemm_epilogue<float>(__uint_as_float(r[j]), p.has_bias, p.alpha, p.beta, bj);
-        }
-        if (vec_ok && col0 + 32 <= p.N) {
-          // stage the warp's 32 x 32 block (row `lane`, 16-byte chunk u at u ^ (lane & 7)),
-          // then write 8 threads x 16 B = 128 contiguous bytes per row, 4 rows at a time
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            *reinterpret_cast<float4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
-          }
-          __syncwarp();
-          const int u = lane & 7;
-#pragma unroll
-          for (int rr = 0; rr < 32; rr += 4) {
-            const int lr = rr + (lane >> 3);
-            const int64_t grow = row_base + lr;
-            const float4 val =
-                *reinterpret_cast<const float4*>(stg + lr * 128 + ((u ^ (lr & 7)) << 4));
-            if (grow < p.M) *reinterpret_cast<float4*>(out + grow * p.ldo + col0 + u * 4) = val;
-          }
-          __syncwarp();
-        } else if (row < p.M) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) out[row * p.ldo + col0 + j] = v[j];
-          }
-        }
+        if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);
     }
   }
 
@@ -445,7 +497,8 @@ static EncodeTiledFn get_encode_fn() {
 // 2-D tensor map over a row-major (rows, cols) fp32 matrix, box (box_cols x box_rows),
 // 128-byte swizzle, zero fill outside the matrix.
 static int make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
-                        int64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
+                        int64_t row_stride, uint32_t box_cols, uint32_t box_rows,
+                        CUtensorMapSwizzle swizzle) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return set_error(BI_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -453,7 +506,7 @@ static int make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return set_error(BI_ERR_INVALID, "cuTensorMapEncodeTiled (fp32) failed (%d) rows=%lld cols=%lld",
@@ -466,10 +519,11 @@ static int make_map_f32(CUtensorMap* map, const void* base, int64_t rows, int64_
 template <bool B_NK>
 static int launch(const GemmArgs& g, cudaStream_t stream) {
   CUtensorMap ma, mb;
-  int st = make_map_f32(&ma, g.a, g.M, g.K, g.lda, BK, BM);
+  int st = make_map_f32(&ma, g.a, g.M, g.K, g.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
-  st = B_NK ? make_map_f32(&mb, g.b, g.N, g.K, g.ldb, BK, BN_CTA)
-            : make_map_f32(&mb, g.b, g.K, g.N, g.ldb, 32, BK);
+  // a (K, N) B is MN-major in shared memory: 128-byte swizzle with 32-byte atoms
+  st = B_NK ? make_map_f32(&mb, g.b, g.N, g.K, g.ldb, BK, BN_CTA, CU_TENSOR_MAP_SWIZZLE_128B)
+            : make_map_f32(&mb, g.b, g.K, g.N, g.ldb, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   if (st) return st;
   auto kern = gemm_tf32x3_kernel<B_NK>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -51,6 +51,26 @@ def test_accuracy_against_float64(bi, b_is_nk):
     assert bi._lib.device_error() == 0
 
 
+@pytest.mark.parametrize("b_is_nk", [True, False])
+def test_error_does_not_grow_with_k(bi, b_is_nk):
+    """The tensor core's fp32 accumulation drifts by a fraction of an ulp per MMA, so one
+    accumulator over all of K let the error grow linearly with K (2.2e-4 at K = 28672).
+    Uniform [0, 1) data, where every product has the same sign, shows it most.  K is summed in
+    256-deep chunks added in fp32 round to nearest: the error stays flat in K (measured
+    ~6e-6 on uniform data at every K from 256 to 28672), inside the reference's float32
+    bar of 2e-5 (tests/test_invariance.py:114-127)."""
+    g = torch.Generator(device="cuda").manual_seed(21)
+    errs = []
+    for K in (256, 4096, 28672):
+        a = torch.rand((17, K), generator=g, device="cuda")
+        b = torch.rand((512, K) if b_is_nk else (K, 512), generator=g, device="cuda")
+        y = bi.linear(a, b) if b_is_nk else bi.matmul(a, b)
+        errs.append(orc.rel_error(to_np(y).astype(np.float64), _exact(a, b, b_is_nk)))
+    assert max(errs) < 1e-5, errs
+    assert errs[-1] < 2.0 * errs[0] + 1e-6, errs  # flat in K, not linear
+    assert bi._lib.device_error() == 0
+
+
 def test_config1_rows_are_batch_invariant(bi):
     """Config 1 in float32 on the tensor-core route: row 0's bits for every M."""
     K = N = 4096
