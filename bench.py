@@ -378,6 +378,9 @@ def run_ours(args):
     ms = _max_over_ranks(ms, world)
     value = FLOPS_PER_STEP * args.steps / (ms / 1e3) / 1e12
 
+    bits_check = _check_against_one_gpu(bi, parallel, xs, ys, world, dev) \
+        if world > 1 else None
+
     nccl_value = None
     if world > 1:
         for _ in range(2):
@@ -564,6 +567,7 @@ def run_ours(args):
         "roofline": roofline,
         "stock_cublas_tflops": cublas_tflops,
         "nccl_allgather_tflops": nccl_value,
+        "fused_vs_single_gpu": bits_check,
         "sdpa": sd,
         "clocks": clk,
     }
@@ -577,6 +581,37 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _check_against_one_gpu(bi, parallel, xs, ys, world, dev):
+    """Bits of the last timed step's gathered outputs against one GPU's result.
+
+    For every shape and every rank's column block, 64 rows spread over all 16 pair tiles
+    of M must equal bi.linear of those rows alone with that block's weight (regenerated
+    here from its seed), computed on this GPU without any exchange: the fused
+    all-gather moves data only, and a row's bits depend neither on M nor on the column
+    block.  Returns the count of differing elements summed over ranks."""
+    rows = sorted({int(r) for r in torch.linspace(0, M - 1, 48).round().tolist()}
+                  | {0, 127, 128, 255, 256, 2047, 2048, M - 256, M - 129, M - 1})
+    ri = torch.tensor(rows, device=dev)
+    diff, checked = 0, 0
+    for i, (K, N) in enumerate(SHAPES):
+        xr = xs[K][ri]
+        for s, e in parallel.shard_bounds(N, world):
+            gw = torch.Generator(device=dev)
+            gw.manual_seed(100 + i)
+            w = (torch.randn((e - s, K), generator=gw, device=dev, dtype=torch.float32)
+                 * 0.02).to(torch.bfloat16)
+            ref = bi.linear(xr, w)
+            got = ys[i][ri, s:e]
+            diff += int((ref.view(torch.int16) != got.view(torch.int16)).sum())
+            checked += ref.numel()
+            del w
+    t = torch.tensor([diff, checked], device=dev, dtype=torch.int64)
+    dist.all_reduce(t)
+    return {"rows": len(rows), "elements_checked": int(t[1]), "elements_differing": int(t[0]),
+            "against": "bi.linear of the sampled rows with each rank's block, one GPU, "
+                       "no exchange"}
 
 
 def _bench_sdpa(bi, parallel, world, rank, dev, peaks, args):

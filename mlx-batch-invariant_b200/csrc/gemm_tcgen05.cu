@@ -28,9 +28,12 @@
 // and the CTA drains what it started, frees TMEM and exits.
 //
 // Fused all-gather (GATHER = true, column-parallel over ranks): the epilogue stores
-// each finished 16-byte chunk into this rank's output and, through NVLink peer
-// mappings (plain stores, no TMA), into every other rank's staging area, where this
-// rank's shard is one dense (M, N_local) row-major block.  A dense block keeps the
+// each finished block into this rank's output and, through NVLink peer mappings, into
+// every other rank's staging area, where this rank's shard is one dense (M, N_local)
+// row-major block.  A full 32 x 128 block leaves the staging buffer by TMA stores (one
+// thread issues them, one box per 64 columns per destination; no multicast), so the
+// epilogue warps go back to the accumulator while the copy engine feeds the links;
+// ragged edges use plain 16-byte or element stores.  A dense block keeps the
 // span of remote addresses in flight small: stores scattered straight into 8 peers'
 // row-major outputs (rows N_total apart) ran 10x slower than the link at 8 GPUs.
 // Each storing thread fences at system scope; the last CTA of the grid (a counter in
@@ -38,6 +41,7 @@
 // release store and waits, bounded, until every rank has posted it.  A second kernel
 // (gather_unpack_kernel) then copies the received blocks into the output.
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -120,7 +124,26 @@ struct Params {
   int tiles_m, tiles_n, num_tiles;
   int group_m;    // pair-tiles of M that consecutive tile indices sweep (L2 reuse of W)
   GatherArgs gx;  // used when GATHER
+  int tma_store;  // GATHER: full staged blocks leave by TMA stores through StoreMaps
 };
+
+// GATHER: where this rank's block goes.  m[d] is rank d's copy of it -- the output
+// itself at d == rank, rank d's staging block otherwise -- as a (N_local, M) 16-bit
+// tensor with a 64 x 32 box and the 128-byte swizzle of the staging buffer.
+struct alignas(64) StoreMaps {
+  CUtensorMap m[BI_MAX_PEERS];
+};
+
+// Byte offset of 16-byte chunk u (0..15, 8 columns each) of row r (0..31) in an
+// epilogue warp's staging buffer.  Plain GEMM: 256-byte rows, chunk u at u ^ (r & 15).
+// GATHER: two 64-column halves of 32 rows x 128 bytes, each in the TMA 128-byte
+// swizzle (chunk u & 7 of row r at (u & 7) ^ (r & 7)), the layout a TMA store reads.
+// Both keep a warp's row-per-lane writes and row-pair reads free of bank conflicts.
+template <bool GATHER>
+__device__ __forceinline__ int stage_off(int r, int u) {
+  if constexpr (GATHER) return ((u >> 3) << 12) + r * 128 + (((u & 7) ^ (r & 7)) << 4);
+  return r * (EPI_COLS * 2) + ((u ^ (r & 15)) << 4);
+}
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m,
                                             int& tm, int& tn) {
@@ -143,7 +166,8 @@ __device__ __forceinline__ uint32_t call_epoch(const GatherArgs& x) {
 template <typename T, bool B_NK, bool GATHER, typename R>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+                   const __grid_constant__ CUtensorMap tmap_b, const Params p,
+                   const __grid_constant__ StoreMaps smap) {
   constexpr int STAGES = R::STAGES;
   constexpr int BN = R::BN;
   constexpr int BN_CTA = R::BN_CTA;
@@ -353,6 +377,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         // Full 128-column halves go through the staging buffer; ragged edges and
         // unaligned outputs take the per-thread path.
         const bool staged = vec_ok && hcol + EPI_COLS <= p.N;
+        if constexpr (GATHER) {
+          // the TMA stores of the previous block have read the buffer
+          if (staged && p.tma_store) {
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+          }
+        }
 #pragma unroll 1
         for (int c = 0; c < EPI_COLS; c += 32) {
           uint32_t r[32];
@@ -377,7 +408,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int u = (c >> 3) + q;
-              *reinterpret_cast<uint4*>(stg + lane * (EPI_COLS * 2) + ((u ^ (lane & 15)) << 4)) =
+              *reinterpret_cast<uint4*>(stg + stage_off<GATHER>(lane, u)) =
                   make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2],
                              packed[4 * q + 3]);
             }
@@ -435,6 +466,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             }
           }
         }
+        if constexpr (GATHER) {
+          if (staged && p.tma_store) {
+            // The staged 32 x 128 block to every rank's copy, own output first: two
+            // 64 x 32 boxes per destination, rows past M clipped by the copy engine.
+            fence_proxy_async_smem();  // the lanes' shared-memory writes, to the async proxy
+            __syncwarp();
+            if (lane == 0 && row_base < p.M) {
+              const int y = static_cast<int>(row_base);
+              for (int j = 0; j < p.gx.world; ++j) {
+                int d = p.gx.rank + j;
+                if (d >= p.gx.world) d -= p.gx.world;
+                tma_store_2d(&smap.m[d], stg, hcol, y);
+                tma_store_2d(&smap.m[d], stg + 4096, hcol + 64, y);
+              }
+              bulk_commit_group();
+            }
+            __syncwarp();
+            continue;
+          }
+        }
         if (staged) {
           // Write the staged 32 x 128 block: two rows per instruction, 16 threads x 16 B
           // = 256 contiguous bytes per row (and per row of each peer's staging block when
@@ -447,7 +498,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const int lr = rr + half_row;
             const int64_t grow = row_base + lr;
             const uint4 v =
-                *reinterpret_cast<const uint4*>(stg + lr * (EPI_COLS * 2) + ((u ^ (lr & 15)) << 4));
+                *reinterpret_cast<const uint4*>(stg + stage_off<GATHER>(lr, u));
             if (grow < p.M) {
               *reinterpret_cast<uint4*>(out + grow * p.ldo + hcol + u * 8) = v;
               if constexpr (GATHER) {
@@ -467,7 +518,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + buf * 8);  // release on the leader
     }
-    if constexpr (GATHER) __threadfence_system();  // this thread's peer stores, before the flag
+    if constexpr (GATHER) {
+      if (p.tma_store && lane == 0) {
+        bulk_wait_all();             // this thread's TMA stores have written everything
+        fence_proxy_async_global();  // ... ordered before its generic-proxy fence below
+      }
+      __syncwarp();
+      __threadfence_system();  // this thread's peer stores, before the flag
+    }
   }
 
   __syncwarp();
@@ -646,6 +704,31 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t co
   return BI_OK;
 }
 
+// GATHER: the maps of the epilogue's TMA stores (see StoreMaps).  False, with nothing
+// reported, when a destination does not meet the copy engine's rules (16-byte aligned
+// base, row pitch a multiple of 16 bytes) -- the epilogue then stores with plain
+// instructions, which write the same bytes.
+static bool make_store_maps(StoreMaps* sm, const GemmArgs& g, const GatherArgs& x) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc || g.M <= 0 || g.N <= 0 || g.N % 8 != 0 || g.ldo % 8 != 0) return false;
+  const int64_t block_off = g.M * x.cols[x.rank];  // elements
+  for (int d = 0; d < x.world; ++d) {
+    void* base = d == x.rank ? g.out
+                             : static_cast<void*>(static_cast<uint16_t*>(x.stages[d]) + block_off);
+    const int64_t pitch = d == x.rank ? g.ldo : g.N;
+    if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g.N), static_cast<cuuint64_t>(g.M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch) * 2};
+    cuuint32_t box[2] = {64, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&sm->m[d], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+  }
+  return true;
+}
+
 // Raster of the persistent schedule: consecutive tile indices walk group_m pair-tiles
 // down M for one column tile before moving along N, so the pairs running at once share
 // a few W column slices in L2.  It decides which pair computes a tile, never a bit.
@@ -687,14 +770,18 @@ static int launch_ring(const GemmArgs& g, const GatherArgs* gx, cudaStream_t str
   p.tiles_n = static_cast<int>((g.N + R::BN - 1) / R::BN);
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.group_m = group_m_for(p.tiles_m);
+  StoreMaps sm;
+  memset(&sm, 0, sizeof(sm));
+  p.tma_store = 0;
   if (gx != nullptr) {
     p.gx = *gx;
+    if (GATHER) p.tma_store = make_store_maps(&sm, g, *gx) ? 1 : 0;
   } else {
     p.gx = GatherArgs{};
   }
   const int max_pairs = device_sm_count() / 2;
   const int pairs = p.num_tiles < max_pairs ? p.num_tiles : max_pairs;
-  kern<<<2 * pairs, NUM_THREADS, R::SMEM_BYTES, stream>>>(ma, mb, p);
+  kern<<<2 * pairs, NUM_THREADS, R::SMEM_BYTES, stream>>>(ma, mb, p, sm);
   return cuda_status(cudaGetLastError(), "gemm_tc launch");
 }
 
