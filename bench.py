@@ -672,7 +672,9 @@ def _bench_sdpa(bi, parallel, world, rank, dev, peaks, args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "traffic": traffic if world == 1 else None,
-                         "kernel": "sdpa_mma_kernel<bf16, D=128, GH=4> (tensor-core route)"},
+                         "kernel": "sdpa_gqa_kernel<bf16, D=128> (GQA route: q.k on the "
+                                   "tensor cores, fold and P.V in fp32; heads per CTA and "
+                                   "ring depth from the grid)"},
             "stock_sdpa_gbs": stock_gbs}
 
 

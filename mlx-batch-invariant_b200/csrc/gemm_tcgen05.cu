@@ -342,7 +342,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter..+31
-    const int row_in_tile = quarter * 32 + lane;
     const T* bias = static_cast<const T*>(p.bias);
     T* out = static_cast<T*>(p.out);
     const bool vec_ok = (p.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);

@@ -782,26 +782,6 @@ constexpr int R = 4;                 // keys per partial per stage
 constexpr int KEYS = PARTIALS * R;   // keys per stage
 constexpr int BOX_D = 64;            // columns per TMA box (128-byte rows)
 
-// Stage ring of STAGES 128-key stages of K and V (the default: one at D = 128, two at
-// D = 64, with two CTAs per SM at 128 registers -- the other CTA's stages cover this
-// one's latency; a deeper ring runs one CTA per SM).  The region before the barriers
-// holds the ring, and after the walk the combine's partials (up to 4 heads x 32
-// partials x D floats, their m / l and denominators).
-template <int D>
-constexpr int default_stages() { return D == 128 ? 1 : 2; }
-
-template <int D, int STAGES_>
-struct Plan {
-  static constexpr int BOXES = D / BOX_D;
-  static constexpr int TSB = KEYS * D * 2;               // one tensor's stage bytes
-  static constexpr int STAGES = STAGES_;
-  static constexpr int COMB = 4 * PARTIALS * D * 4 + 2 * 4 * PARTIALS * 4 + 64;
-  static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
-  static constexpr int SMEM = 1024 + REGION + STAGES * 8 + 64;
-  static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
-  static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
-};
-
 template <typename T>
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -824,12 +804,6 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
                : "r"(addr));
 }
 
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
 // Shared-memory address of the 16-byte chunk holding columns [d, d + 8) of stage row
 // `row`: one TMA box per 64 columns (KEYS rows of 128 B), chunks swizzled by row % 8.
 __device__ __forceinline__ uint32_t kv_addr(uint32_t base, int row, int d) {
@@ -838,60 +812,98 @@ __device__ __forceinline__ uint32_t kv_addr(uint32_t base, int row, int d) {
   return base + box * (KEYS * 128) + row * 128 + ((c ^ (row & 7)) << 4);
 }
 
-// Two fp32 values -> one register of two 16-bit T (round to nearest even), and what
-// the rounding left over.
+// ---------------------------------------------------------------------------------
+// GQA kernel: q.k on the tensor cores, the fold and P.V on the CUDA cores.
+//
+// One CTA per (batch, query row, GH = 4, 2 or 1 query heads of one KV head), 256
+// threads, 128-key stages.  Thread (p, sl) -- p = tid / 8 the partial, sl = tid % 8 --
+// owns, for the GH heads, o[h][d] of partial p for the columns d = 64 c + 8 sl + [0, 8).
+// Per stage t:
+//   A. scores: warp w computes S[key][head] = k_key . q_head for keys 16w .. 16w+15
+//      as one m16n8k16 MMA chain over the head dim (A = 16 K rows from shared memory,
+//      B = the GH q rows -- the other columns zero), fp32 accumulation, into shared
+//      memory.  Every K fragment serves all GH heads.
+//   B. fold: the 8 threads of partial p hold its GH x 4 (head, key) pairs of the stage
+//      (keys 32 j + p; 8 / GH threads per head: two keys each for GH = 4, one for GH =
+//      2, one twice over for GH = 1) and, per head, the state (m, l) in each of them:
+//          x_j = scale * S (+ mask),  m' = max(m, max_j x_j),  e_j = exp(x_j - m'),
+//          f = exp(m - m'),  l = fmaf(l, f, (e_0 + e_1) + (e_2 + e_3)),
+//      the max and the two pair sums crossing the head's threads by shuffle; the
+//      weights reach the other threads of the partial by shuffle (-0.0 marks a key
+//      that is not visible: exp never returns it).
+//   C. numerator: o = o * f (skipped when f == 1), then o = fmaf(e_j, v_j, o) for the
+//      visible keys j = 0..3 in order, in fp32 (packed fma.rn.f32x2): the weights
+//      enter exactly.  Each V row is read once for the 4 heads.
+// With OVERLAP (a ring of two or more stages), A of stage t + 1 runs right after C of
+// stage t (scores double-buffered), so one CTA-wide barrier per stage remains.  A row's
+// arithmetic depends on its own q row, the keys and the mask only: an MMA column is
+// one head whatever the others hold, and every other step is per (head, partial).  GH,
+// the ring depth and OVERLAP decide which CTA, thread, buffer and barrier run a step,
+// never the step.
+template <int D, int GH_, int S_, bool OVERLAP_>
+struct GqaPlan {
+  static constexpr int GH = GH_;
+  static constexpr int NT = 256;
+  static constexpr int NCH = D / 64;        // 16-byte V vectors per thread per key
+  static constexpr int TSB = KEYS * D * 2;  // one tensor's stage bytes
+  static constexpr int STAGES = S_;
+  static constexpr bool OVERLAP = OVERLAP_;
+  static_assert(!OVERLAP_ || S_ >= 2, "overlap needs a second stage");
+  static constexpr int XP = KEYS + 8;       // score row pitch (distinct banks for phase B)
+  static constexpr int XBUF = OVERLAP ? 2 : 1;
+  static constexpr int COMB = GH * PARTIALS * D * 4 + 2 * GH * PARTIALS * 4 + 64;
+  static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
+  static constexpr int SMEM = 1024 + REGION + XBUF * GH * XP * 4 + STAGES * 8 + 64;
+  static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
+  static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
+};
+
+// 8 consecutive 16-bit values -> 4 fp32 pairs (exact).
 template <typename T>
-__device__ __forceinline__ uint32_t pack_rn(float lo, float hi, float& rlo, float& rhi) {
-  uint32_t r;
-  if constexpr (dtype_of<T>::value == 2) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    rlo = __fsub_rn(lo, __low2float(v));
-    rhi = __fsub_rn(hi, __high2float(v));
-    r = *reinterpret_cast<const uint32_t*>(&v);
-  } else {
-    const __half2 v = __floats2half2_rn(lo, hi);
-    rlo = __fsub_rn(lo, __low2float(v));
-    rhi = __fsub_rn(hi, __high2float(v));
-    r = *reinterpret_cast<const uint32_t*>(&v);
+__device__ __forceinline__ void widen8(const uint4 x, f2 (&v)[4]) {
+  const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (dtype_of<T>::value == 2) {
+      v[i] = pack2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      v[i] = pack2(f.x, f.y);
+    }
   }
-  return r;
 }
 
-template <typename T>
-__device__ __forceinline__ uint32_t pack_rn(float lo, float hi) {
-  float a, b;
-  return pack_rn<T>(lo, hi, a, b);
-}
+constexpr uint32_t kHiddenKey = 0x80000000u;  // -0.0f: the weight of a key not visible
 
-template <typename T, int D, int GH, int S>
-__global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
-    sdpa_mma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+template <typename T, int D, int GH_, int S, bool OV>
+__global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
+    sdpa_gqa_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const Params p) {
-  using PL = Plan<D, S>;
-  constexpr int NW = 2 * GH;         // warps: 16 MMA rows each
-  constexpr int NT = 32 * NW;
-  constexpr int NPW = 16 / GH;       // partials per warp
-  constexpr int KG = NPW / 4;        // 16-key MMA steps per warp per stage
-  constexpr int KSTEPS = D / 16;     // MMA k-steps over the head dim
-  constexpr int NTD = D / 8;         // n-tiles of the output row
+  using PL = GqaPlan<D, GH_, S, OV>;
+  constexpr int GH = PL::GH;
+  constexpr int NT = PL::NT;
+  constexpr int NCH = PL::NCH;
+  constexpr int KSTEPS = D / 16;  // MMA k-steps over the head dim
   constexpr int STAGES = PL::STAGES;
   constexpr int TSB = PL::TSB;
-  static_assert(KSTEPS % 2 == 0 && NTD % 2 == 0, "fragments are loaded in pairs");
+  constexpr int XP = PL::XP;
+  constexpr bool OVERLAP = PL::OVERLAP;
+  static_assert(NT / 32 * 16 == KEYS, "one 16-key MMA tile per warp");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + STAGES * TSB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PL::REGION);
-  int* done_count = reinterpret_cast<int*>(full + STAGES);
-  int* issued_count = done_count + STAGES;
-  volatile int* abort_flag = issued_count + 1;
+  float* xs = reinterpret_cast<float*>(smem + PL::REGION);  // scores [XBUF][GH][XP]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + PL::XBUF * GH * XP);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + STAGES);
+  int* issued_count = const_cast<int*>(abort_flag) + 1;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int gq = lane >> 2;  // MMA group: this thread's rows gq and gq + 8
+  const int gq = lane >> 2;
   const int q4 = lane & 3;
 
   const int groups = p.H / GH;
@@ -910,60 +922,86 @@ __global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
   }
   const int nblocks = static_cast<int>((kmax + KEYS - 1) / KEYS);
 
-  // This thread's two rows: same head, partials part[0] and part[1].
-  const int head = gq % GH;
-  int pp[2] = {gq / GH, (gq + 8) / GH};
-  int part[2] = {warp * NPW + pp[0], warp * NPW + pp[1]};
-
-  const T* Q = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.qs0 +
-               static_cast<int64_t>(h0 + head) * p.qs1 + static_cast<int64_t>(s) * p.qs2;
-  uint32_t qa[KSTEPS][2];
+  // Phase A operand: q of head gq (columns 4..7 of B are zero).
+  uint32_t qb[KSTEPS][2];
+  {
+    const T* Q = static_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.qs0 +
+                 static_cast<int64_t>(h0 + (gq < GH ? gq : 0)) * p.qs1 +
+                 static_cast<int64_t>(s) * p.qs2;
 #pragma unroll
-  for (int kk = 0; kk < KSTEPS; ++kk) {
-    qa[kk][0] = *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 2 * q4);
-    qa[kk][1] = *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 8 + 2 * q4);
-  }
-  const T* Mk = static_cast<const T*>(p.mask);
-  const T* mrow = Mk == nullptr ? nullptr
-                                : Mk + static_cast<int64_t>(b) * p.ms0 +
-                                      static_cast<int64_t>(h0 + head) * p.ms1 +
-                                      static_cast<int64_t>(s) * p.ms2;
-
-  float o[NTD][4];
-#pragma unroll
-  for (int nd = 0; nd < NTD; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
-  float m[2] = {-3.40282347e+38f, -3.40282347e+38f};
-  float l[2] = {0.f, 0.f};
-  const T* Sk = static_cast<const T*>(p.sinks);
-  if (Sk != nullptr) {
-#pragma unroll
-    for (int ri = 0; ri < 2; ++ri) {
-      if (part[ri] == 0) {
-        m[ri] = to_f32(Sk[h0 + head]);
-        l[ri] = 1.f;
-      }
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      qb[kk][0] = gq < GH ? *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 2 * q4) : 0u;
+      qb[kk][1] = gq < GH ? *reinterpret_cast<const uint32_t*>(Q + 16 * kk + 8 + 2 * q4) : 0u;
     }
   }
+  // Phases B and C: partial cp; in B head bh, keys of index wi among the head's TPH.
+  constexpr int TPH = 8 / GH;           // threads per head in a partial's 8
+  constexpr int KPT = GH == 4 ? 2 : 1;  // keys per thread in B
+  const int cp = tid >> 3;
+  const int sl = tid & 7;
+  const int bh = sl / TPH;
+  const int wi = sl % TPH;
+  const int grp = lane & ~7;  // first lane of this partial's 8
+  float m = -3.40282347e+38f, l = 0.f;  // state of (head bh, partial cp), in each of its threads
+  {
+    const T* Sk = static_cast<const T*>(p.sinks);
+    if (Sk != nullptr && cp == 0) {
+      m = to_f32(Sk[h0 + bh]);
+      l = 1.f;
+    }
+  }
+  const T* mrow = p.mask_mode == 2
+                      ? static_cast<const T*>(p.mask) + static_cast<int64_t>(b) * p.ms0 +
+                            static_cast<int64_t>(h0 + bh) * p.ms1 + static_cast<int64_t>(s) * p.ms2
+                      : nullptr;
+  f2 o[GH][NCH][4];
+#pragma unroll
+  for (int h = 0; h < GH; ++h)
+#pragma unroll
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[h][c][i] = pack2(0.f, 0.f);
 
   auto issue = [&](int blk) {
     const int st = blk % STAGES;
     mbar_arrive_expect_tx(&full[st], 2 * TSB);
 #pragma unroll
-    for (int bx = 0; bx < PL::BOXES; ++bx) {
-      tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh,
-                  b);
-      tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh,
-                  b);
+    for (int bx = 0; bx < D / BOX_D; ++bx) {
+      tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh, b);
+      tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh, b);
     }
+  };
+  // A: scores of stage block t (its K in ring slot t % STAGES) into buffer xb.
+  auto scores = [&](int t, float* xb) {
+    const uint32_t kbase = smem_u32(sK + (t % STAGES) * TSB);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    const int mi = lane >> 3;
+    const int krow = 16 * warp + (lane & 7) + 8 * (mi & 1);
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, kv_addr(kbase, krow, 16 * kk + 8 * (mi >> 1)));
+      mma16816<T>(c, a[0], a[1], a[2], a[3], qb[kk][0], qb[kk][1]);
+    }
+    // columns 2 q4, 2 q4 + 1 are heads (those below GH); rows gq and gq + 8 keys
+    const int k0 = 16 * warp + gq;
+    if (2 * q4 < GH) {
+      xb[(2 * q4) * XP + k0] = c[0];
+      xb[(2 * q4) * XP + k0 + 8] = c[2];
+    }
+    if (2 * q4 + 1 < GH) {
+      xb[(2 * q4 + 1) * XP + k0] = c[1];
+      xb[(2 * q4 + 1) * XP + k0 + 8] = c[3];
+    }
+  };
+  auto wait_stage = [&](int t) {
+    return mbar_wait(&full[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
   };
 
   if (tid == 0) {
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    for (int st = 0; st < STAGES; ++st) {
-      mbar_init(&full[st], 1);
-      done_count[st] = 0;
-    }
+    for (int st = 0; st < STAGES; ++st) mbar_init(&full[st], 1);
     *abort_flag = 0;
     fence_barrier_init();
     int n0 = 0;
@@ -974,137 +1012,143 @@ __global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
 
   const float scale = p.scale;
   bool aborted = false;
+  bool ok = true;
+  if constexpr (OVERLAP) {
+    if (nblocks > 0) {
+      ok = wait_stage(0);
+      if (ok) scores(0, xs);
+    }
+  }
   for (int t = 0; t < nblocks; ++t) {
     const int st = t % STAGES;
-    bool ok = mbar_wait(&full[st], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok) {
-      if (lane == 0) {
+    float* xb = xs + (OVERLAP ? (t & 1) * GH * XP : 0);
+    if constexpr (!OVERLAP) {
+      ok = wait_stage(t);
+      if (ok) scores(t, xb);
+    }
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
         *abort_flag = 1;
         record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
       }
       aborted = true;
       break;
     }
-    const uint32_t kbase = smem_u32(sK + st * TSB);
-    const uint32_t vbase = smem_u32(sV + st * TSB);
-    const int64_t key0 = static_cast<int64_t>(t) * KEYS;
-#pragma unroll
-    for (int g = 0; g < KG; ++g) {
-      const int pbase = warp * NPW + 4 * g;  // first partial of this MMA step
-      // ---- scores: 16 rows x 16 key positions (position = 4 * j + partial % 4)
-      float sc[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-        const int pos = 8 * nt + (lane & 7);
-        const int krow = 32 * (pos >> 2) + pbase + (pos & 3);
-        const int mi = lane >> 3;
-#pragma unroll
-        for (int kk = 0; kk < KSTEPS; kk += 2) {
-          uint32_t bf[4];
-          ldsm_x4(bf, kv_addr(kbase, krow, 16 * (kk + (mi >> 1)) + 8 * (mi & 1)));
-          mma16816<T>(sc[nt], qa[kk][0], qa[kk][0], qa[kk][1], qa[kk][1], bf[0], bf[1]);
-          mma16816<T>(sc[nt], qa[kk + 1][0], qa[kk + 1][0], qa[kk + 1][1], qa[kk + 1][1], bf[2],
-                      bf[3]);
-        }
-      }
-      // ---- stage update of each of this thread's rows whose partial is in this step.
-      // Element (nt, e) of row ri is position 8*nt + 2*q4 + e; it is one of the row's
-      // keys when that position % 4 == the row's partial % 4, i.e. when
-      // (q4 & 1) == want >> 1 and e == want & 1; its j is 2*nt + (q4 >> 1).
-      uint32_t phi[4], plo[4];
-#pragma unroll
-      for (int ri = 0; ri < 2; ++ri) {
-        const bool mine = (pp[ri] >> 2) == g;
-        const int want = pp[ri] & 3;
-        const bool holder = mine && (q4 & 1) == (want >> 1);
-        float x[2];
-        bool use[2];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int j = 2 * nt + (q4 >> 1);
-          const int64_t key = key0 + 32 * j + pbase + want;
-          bool u = holder && key < kmax;
-          float v = __fmul_rn(sc[nt][2 * ri + (want & 1)], scale);
-          if (u && p.mask_mode == 2) {
-            const float bias = to_f32(mrow[key]);
-            u = bias > -3.0e38f;
-            v = __fadd_rn(v, bias);
-          }
-          use[nt] = u;
-          x[nt] = v;
-        }
-        float mx = use[0] ? x[0] : -INFINITY;
-        if (use[1]) mx = fmaxf(mx, x[1]);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        // Whether some key of the row is visible is uniform over the quad, not over the
-        // warp, so every shuffle below runs unconditionally and only the state update
-        // is guarded.
-        const bool any = mx != -INFINITY;
-        const float mn = any ? fmaxf(m[ri], mx) : m[ri];
-        float e[2];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) e[nt] = use[nt] ? expf(__fsub_rn(x[nt], mn)) : 0.f;
-        // (e_0 + e_1) + (e_2 + e_3): j = 2*nt + (q4 >> 1); lanes q4 and q4 ^ 2 hold
-        // j and j ^ 1 of the same nt.
-        const float u0 = __fadd_rn(e[0], __shfl_xor_sync(0xffffffffu, e[0], 2));
-        const float u1 = __fadd_rn(e[1], __shfl_xor_sync(0xffffffffu, e[1], 2));
-        const float sum =
-            __shfl_sync(0xffffffffu, __fadd_rn(u0, u1), (lane & ~3) | (want >> 1));
-        if (any) {
-          const float f = mn == m[ri] ? 1.0f : expf(__fsub_rn(m[ri], mn));
-          l[ri] = __fmaf_rn(l[ri], f, sum);
-          if (f != 1.0f) {
-#pragma unroll
-            for (int nd = 0; nd < NTD; ++nd) {
-              o[nd][2 * ri] = __fmul_rn(o[nd][2 * ri], f);
-              o[nd][2 * ri + 1] = __fmul_rn(o[nd][2 * ri + 1], f);
-            }
-          }
-          m[ri] = mn;
-        }
-        // this row's weights at its positions (nt, e = want & 1), zero elsewhere
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const float w0 = (want & 1) == 0 ? e[nt] : 0.f;
-          const float w1 = (want & 1) == 1 ? e[nt] : 0.f;
-          float r0, r1;
-          phi[2 * nt + ri] = pack_rn<T>(w0, w1, r0, r1);
-          plo[2 * nt + ri] = pack_rn<T>(r0, r1);
-        }
-      }
-      // ---- o += P V over this step's 16 keys (P = P_hi + P_lo)
-      const int mi = lane >> 3;
-      const int vpos = 8 * (mi & 1) + (lane & 7);
-      const int vrow = 32 * (vpos >> 2) + pbase + (vpos & 3);
-#pragma unroll
-      for (int nd = 0; nd < NTD; nd += 2) {
-        uint32_t bv[4];
-        ldsm_x4_t(bv, kv_addr(vbase, vrow, 8 * (nd + (mi >> 1))));
-        mma16816<T>(o[nd], phi[0], phi[1], phi[2], phi[3], bv[0], bv[1]);
-        mma16816<T>(o[nd], plo[0], plo[1], plo[2], plo[3], bv[0], bv[1]);
-        mma16816<T>(o[nd + 1], phi[0], phi[1], phi[2], phi[3], bv[2], bv[3]);
-        mma16816<T>(o[nd + 1], plo[0], plo[1], plo[2], plo[3], bv[2], bv[3]);
+    if constexpr (OVERLAP) {
+      // every warp is done with block t - 1 (its C) and with this block's A: refill
+      if (tid == 0 && t >= 1 && t - 1 + STAGES < nblocks) {
+        fence_proxy_async_smem();
+        issue(t - 1 + STAGES);
+        *issued_count = t - 1 + STAGES + 1;
       }
     }
-    // The last warp done with this stage refills it with block t + STAGES.
-    __syncwarp();
-    if (lane == 0) {
-      __threadfence_block();
-      if (atomicAdd(&done_count[st], 1) == NW - 1) {
-        __threadfence_block();
-        done_count[st] = 0;
-        if (t + STAGES < nblocks && !*abort_flag) {
-          fence_proxy_async_smem();
-          issue(t + STAGES);
-          atomicMax(issued_count, t + STAGES + 1);
+    const int64_t key0 = static_cast<int64_t>(t) * KEYS;
+
+    // ---- B: head bh, keys j(u) of partial cp
+    float x[KPT];
+    bool use[KPT];
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) {
+      const int j = GH == 4 ? 2 * wi + u : (wi & 3);
+      const int64_t key = key0 + 32 * j + cp;
+      bool vis = key < kmax;
+      float v = __fmul_rn(xb[bh * XP + 32 * j + cp], scale);
+      if (vis && mrow != nullptr) {
+        const float bias = to_f32(mrow[key]);
+        vis = bias > -3.0e38f;
+        v = __fadd_rn(v, bias);
+      }
+      use[u] = vis;
+      x[u] = v;
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < KPT; ++u)
+      if (use[u]) mx = fmaxf(mx, x[u]);
+    // the head's 4 keys sit in lanes differing in bit 0 (GH = 4) or bits 0-1
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if (GH < 4) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const bool any = mx != -INFINITY;
+    const float mn = any ? fmaxf(m, mx) : m;
+    float ev[KPT];
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) ev[u] = use[u] ? expf(__fsub_rn(x[u], mn)) : __uint_as_float(kHiddenKey);
+    const float e0 = ev[0];
+    const float e1 = ev[KPT - 1];
+    // (e_0 + e_1) + (e_2 + e_3); IEEE addition is commutative, so every thread of the
+    // head gets the same sum whichever half it holds
+    float pair;
+    if (GH == 4) {
+      pair = __fadd_rn(use[0] ? e0 : 0.f, use[KPT - 1] ? e1 : 0.f);
+    } else {
+      const float mine = use[0] ? e0 : 0.f;
+      pair = __fadd_rn(mine, __shfl_xor_sync(0xffffffffu, mine, 1));
+    }
+    const float pair_other = __shfl_xor_sync(0xffffffffu, pair, GH == 4 ? 1 : 2);
+    float f = 1.0f;
+    if (any) {
+      const float sum = __fadd_rn(pair, pair_other);
+      f = mn == m ? 1.0f : expf(__fsub_rn(m, mn));
+      l = __fmaf_rn(l, f, sum);
+      m = mn;
+    }
+
+    // ---- C: o = o * f, then o = fmaf(e_j, v_j, o) for the visible keys, j ascending
+    const uint32_t vbase = smem_u32(sV + st * TSB);
+#pragma unroll
+    for (int h = 0; h < GH; ++h) {
+      const float fh = __shfl_sync(0xffffffffu, f, grp + TPH * h);
+      if (fh != 1.0f) {
+        const f2 ff = pack2(fh, fh);
+#pragma unroll
+        for (int c2 = 0; c2 < NCH; ++c2)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[h][c2][i] = mul2(o[h][c2][i], ff);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      f2 v[NCH][4];
+#pragma unroll
+      for (int c2 = 0; c2 < NCH; ++c2) {
+        uint4 raw;
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
+                     : "r"(kv_addr(vbase, 32 * j + cp, 64 * c2 + 8 * sl)));
+        widen8<T>(raw, v[c2]);
+      }
+      // weight of (head h, key j): GH = 4: thread 2 h + j / 2 of the partial, its
+      // e_{j % 2}; else thread TPH h + j
+      const float mine = (GH == 4 && (j & 1)) ? e1 : e0;
+#pragma unroll
+      for (int h = 0; h < GH; ++h) {
+        const float eh =
+            __shfl_sync(0xffffffffu, mine, grp + TPH * h + (GH == 4 ? (j >> 1) : j));
+        if (__float_as_uint(eh) != kHiddenKey) {
+          const f2 ee = pack2(eh, eh);
+#pragma unroll
+          for (int c2 = 0; c2 < NCH; ++c2)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[h][c2][i] = fma2(ee, v[c2][i], o[h][c2][i]);
         }
+      }
+    }
+
+    if constexpr (OVERLAP) {
+      if (t + 1 < nblocks) {
+        ok = wait_stage(t + 1);
+        if (ok) scores(t + 1, xs + ((t + 1) & 1) * GH * XP);
+      }
+    } else {
+      __syncthreads();  // stage st and the scores are free
+      if (tid == 0 && t + STAGES < nblocks && !*abort_flag) {
+        fence_proxy_async_smem();
+        issue(t + STAGES);
+        *issued_count = t + STAGES + 1;
       }
     }
   }
-  if (__syncthreads_or(aborted)) {
+  if (aborted) {
     if (tid == 0) {
       const int issued = *issued_count;
       for (int blk = issued - STAGES < 0 ? 0 : issued - STAGES; blk < issued; ++blk) {
@@ -1115,23 +1159,26 @@ __global__ void __launch_bounds__(64 * GH, (Plan<D, S>::CTAS_PER_SM))
   }
   __syncthreads();  // every stage consumed and no copy in flight: the ring is free
 
-  // ---- combine the 32 partials of every head, p = 0..31
-  float* comb_o = reinterpret_cast<float*>(smem);               // [GH][32][D]
-  float* comb_m = comb_o + GH * PARTIALS * D;                   // [GH][32]
-  float* comb_l = comb_m + GH * PARTIALS;                       // [GH][32]
+  // ---- combine the 32 partials of every head, p = 0..31 (as the CUDA-core route)
+  float* comb_o = reinterpret_cast<float*>(smem);  // [GH][32][D]
+  float* comb_m = comb_o + GH * PARTIALS * D;      // [GH][32]
+  float* comb_l = comb_m + GH * PARTIALS;          // [GH][32]
+  float* comb_s = comb_l + GH * PARTIALS;          // [GH] denominators
 #pragma unroll
-  for (int ri = 0; ri < 2; ++ri) {
-    float* row = comb_o + (head * PARTIALS + part[ri]) * D;
+  for (int h = 0; h < GH; ++h) {
 #pragma unroll
-    for (int nd = 0; nd < NTD; ++nd) {
-      *reinterpret_cast<float2*>(row + 8 * nd + 2 * q4) = make_float2(o[nd][2 * ri], o[nd][2 * ri + 1]);
-    }
-    if (q4 == 0) {
-      comb_m[head * PARTIALS + part[ri]] = m[ri];
-      comb_l[head * PARTIALS + part[ri]] = l[ri];
+    for (int c2 = 0; c2 < NCH; ++c2) {
+      float4* dst = reinterpret_cast<float4*>(comb_o + (h * PARTIALS + cp) * D + 64 * c2 + 8 * sl);
+      dst[0] = make_float4(lo_of(o[h][c2][0]), hi_of(o[h][c2][0]), lo_of(o[h][c2][1]),
+                           hi_of(o[h][c2][1]));
+      dst[1] = make_float4(lo_of(o[h][c2][2]), hi_of(o[h][c2][2]), lo_of(o[h][c2][3]),
+                           hi_of(o[h][c2][3]));
     }
   }
-  float* comb_s = comb_l + GH * PARTIALS;                       // [GH] denominators
+  if (wi == 0) {
+    comb_m[bh * PARTIALS + cp] = m;
+    comb_l[bh * PARTIALS + cp] = l;
+  }
   __syncthreads();
   if (warp < GH) {
     const float ls = combine_weights(comb_m + warp * PARTIALS, comb_l + warp * PARTIALS, lane);
@@ -1268,54 +1315,67 @@ static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], co
   return encode_tiled16(map, base, 4, dims, strides, box, a.dtype);
 }
 
-template <typename T, int D, int GH, int S = default_stages<D>()>
-static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  using PL = Plan<D, S>;
+template <typename T, int D, int GH, int S, bool OV>
+static int launch_gqa(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
+  using PL = GqaPlan<D, GH, S, OV>;
   CUtensorMap tk, tv;
   int st = kv_map<D>(&tk, a.k, a.ks, a);
   if (st) return st;
   st = kv_map<D>(&tv, a.v, a.vs, a);
   if (st) return st;
-  auto kern = sdpa_mma_kernel<T, D, GH, S>;
+  auto kern = sdpa_gqa_kernel<T, D, GH, S, OV>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        PL::SMEM);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa tc)");
-  const int64_t blocks = a.B * (a.H / GH) * a.qL;
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa gqa)");
+  const int64_t blocks = a.B * (a.H / PL::GH) * a.qL;
   if (blocks > 0x7fffffffLL) return set_error(BI_ERR_UNSUPPORTED, "too many attention rows");
-  kern<<<static_cast<unsigned>(blocks), 64 * GH, PL::SMEM, stream>>>(tk, tv, p);
-  return cuda_status(cudaGetLastError(), "sdpa tc launch");
+  kern<<<static_cast<unsigned>(blocks), PL::NT, PL::SMEM, stream>>>(tk, tv, p);
+  return cuda_status(cudaGetLastError(), "sdpa gqa launch");
 }
 
-// Query heads per CTA (GH) and ring depth (S) for a grid of B * H / GH * qL CTAs.  Each
-// (head, partial) is one MMA row whose value depends only on its own q row and the key
-// columns, whatever the other rows hold, and the ring only stages keys, so both decide
-// which CTA computes a row and how its keys arrive -- never the row's bits.
-struct TcPlan {
-  int gh, stages;
-};
-
-// Four heads per CTA always (2 or 1 repeat the key-side MMAs per head: measured 1.5-4x
-// slower).  A grid with no more CTAs than SMs (decode on a head shard: 4 and 8 GPUs at
-// the bench shape) runs one CTA per SM with a 3-stage ring -- 4.9 vs 3.2 TB/s at
-// B = 64, H = 8, Hkv = 2 -- otherwise two CTAs per SM cover each other's latency.
-static TcPlan tc_plan(const SdpaArgs& a, int sms) {
-  const int64_t ctas = a.B * (a.H / 4) * a.qL;
-  return TcPlan{4, ctas <= sms ? 3 : 0};
+// Heads per CTA and ring depth: GH = 4 shares each K/V stage between four heads; a grid
+// with few CTAs takes GH = 2 or 1 (the next GH while twice the CTAs still fit on the
+// SMs), which puts more SMs on the same keys (a KV head's stages then arrive once per
+// CTA, mostly from L2).  D = 128: a grid with more CTAs than SMs runs two 1-stage CTAs
+// per SM (each covers the other's load latency), a smaller one a 3-stage ring per SM;
+// D = 64: always the 3-stage ring with A of the next stage overlapping, two CTAs per
+// SM.  Measured on B200 (decode, L = 8192): GH = 2 with two 1-stage CTAs per SM for a
+// 512-row grid ran 160 us against 139 us for GH = 4 with one 3-stage CTA per SM; the
+// overlap gained at D = 64 (229 vs 232 us) and not at D = 128.  None of these changes a
+// row's bits.
+template <typename T, int D, int GH>
+static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream, bool big) {
+  if (big) return launch_gqa<T, D, GH, 1, false>(a, p, stream);
+  return launch_gqa<T, D, GH, 3, D == 64>(a, p, stream);
 }
 
 template <typename T, int D>
 static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  const TcPlan pl = tc_plan(a, device_sm_count());
-  const bool deep = pl.stages > default_stages<D>();
-  (void)pl.gh;  // the kernel also builds for 1 or 2 heads per CTA; 4 is the one routed
-  return deep ? launch_gh<T, D, 4, 3>(a, p, stream) : launch_gh<T, D, 4>(a, p, stream);
+  const int64_t sms = device_sm_count();
+  const int64_t rows = a.B * a.H * a.qL;  // query (row, head) pairs
+  int gh = 4;
+  bool big;
+  if (D == 64) {
+    // 3-stage CTAs fit two per SM
+    while (gh > 1 && 2 * (rows / gh) <= 2 * sms) gh /= 2;
+    big = false;
+  } else if (rows / 4 > sms) {
+    big = true;  // two 1-stage CTAs per SM
+  } else {
+    while (gh > 1 && 2 * (rows / gh) <= sms) gh /= 2;
+    big = false;  // one 3-stage CTA per SM
+  }
+  if (gh == 4) return launch_gh<T, D, 4>(a, p, stream, big);
+  if (gh == 2) return launch_gh<T, D, 2>(a, p, stream, big);
+  return launch_gh<T, D, 1>(a, p, stream, big);
 }
 
 }  // namespace tcr
 
 // Route: fp16 / bf16 with D = 64 or 128 and every KV head shared by a multiple of 4
-// query heads take the tensor-core kernel (its MMA rows are the 4 heads x partials, so
-// each K/V fragment serves 4 rows); everything else the CUDA-core one.  The route is a
+// query heads take the GQA kernel (its q.k MMAs serve the 4 heads from each K
+// fragment, its fold and P.V read each V row once for them); everything else the
+// CUDA-core one.  The route is a
 // function of the model's shapes (dtype, D, H / Hkv) only -- never of B, qL or N -- so
 // a token's bits are the same in decode and in any chunked prefill.
 template <typename T>

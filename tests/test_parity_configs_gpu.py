@@ -13,9 +13,9 @@ CUDA-core route, which runs the oracle's K order: bit-exact.
 
 Attention bar (every sampled element): conftest.attn_worst -- within half an output
 ulp of the oracle's unrounded fp32 result plus tau * sum_i p_i |v_ij| / sum_i p_i, with
-tau = 2^-20 on the CUDA-core route and 2^-16 on the tensor-core route, whose three
-departures from the reference's per-key fold (score = scale * (q . k), keys folded 4
-at a time, weights as e_hi + e_lo) each move a weight by a few 2^-19 relative at most.
+tau = 2^-20 on both routes (the GQA route departs from the reference's per-key fold in
+two places -- score = scale * (q . k) from a tensor-core dot product, keys folded 4 at
+a time -- and runs P.V in exact fp32).
 """
 
 import math

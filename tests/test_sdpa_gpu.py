@@ -3,10 +3,10 @@
 Parity bar against the host oracle (the reference's per-key fold), elementwise
 (conftest.attn_worst): every output element within half an output ulp of the oracle's
 unrounded fp32 result (2 fp32 ulps for float32) plus tau * sum_i p_i |v_ij| / sum_i p_i,
-tau = 2^-20 on the CUDA-core route (the oracle's fold, lane split and order; C-library
-expf in place of CUDA's) and 2^-16 on the tensor-core route (16-bit, D = 64 / 128, GQA
-groups of 4k heads: score = scale * (q . k), a partial's keys folded 4 at a time,
-weights entering P.V as e_hi + e_lo).
+tau = 2^-20 on both routes: the CUDA-core one runs the oracle's fold, lane split and
+order (C-library expf in place of CUDA's); the GQA one (16-bit, D = 64 / 128, GQA groups
+of 4k heads) takes score = scale * (q . k) from a tensor-core dot product and folds a
+partial's keys 4 at a time, with P.V in exact fp32.
 Accuracy against float64 follows the reference (tests/test_invariance.py:408-432):
 float32 < 2e-6, bfloat16 < 3e-2.  Invariance bar: 0 differing bits.
 """
@@ -177,6 +177,30 @@ def test_decode_batch_and_kv_length_invariance_c2(bi, dtype):
             keep3[..., :L] = True
             ext3 = bi.scaled_dot_product_attention(q1, k3, v3, mask=keep3)
             assert np.array_equal(bits(ext3), bits(plain)), dtype
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("D", [64, 128])
+def test_gqa_launch_plans_keep_the_bits(bi, dtype, D):
+    """The GQA kernel takes 1, 2 or 4 query heads per CTA and a 1- or 3-stage ring from
+    the grid size (B * H * qL against the SM count); none of it may change a row.  With
+    H = 32, Hkv = 8 the batches below run GH = 1 (B <= 4), GH = 2 (B = 8) and GH = 4
+    (B >= 16, one or two CTAs per SM): slot 0's bits must not move."""
+    H, Hkv, L = 32, 8, 1500
+    q1 = randn((1, H, 1, D), dtype, 31, "cuda")
+    k1 = randn((1, Hkv, L, D), dtype, 32, "cuda")
+    v1 = randn((1, Hkv, L, D), dtype, 33, "cuda")
+    sinks = randn((H,), dtype, 34, "cuda")
+    base = None
+    for B in (1, 3, 8, 16, 40, 64):
+        q = torch.cat([q1, randn((B - 1, H, 1, D), dtype, 400 + B, "cuda")]) if B > 1 else q1
+        k = torch.cat([k1, randn((B - 1, Hkv, L, D), dtype, 500 + B, "cuda")]) if B > 1 else k1
+        v = torch.cat([v1, randn((B - 1, Hkv, L, D), dtype, 600 + B, "cuda")]) if B > 1 else v1
+        got = bits(bi.scaled_dot_product_attention(q, k, v, mask="causal", sinks=sinks)[0])
+        if base is None:
+            base = got
+        else:
+            assert int((got != base).sum()) == 0, (dtype, D, B)
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
