@@ -7,10 +7,11 @@
 // Each partial keeps an fp32 online-softmax state (running max m, denominator l,
 // numerator o[V]); the 32 partials are then combined in the fixed order p = 0..31.
 // Nothing depends on B, qL, N or on the other rows in flight: there is no split-KV,
-// no second pass, and the route (the CUDA-core kernel here, or the tensor-core kernel
-// further down for 16-bit data with D = 64 / 128 and GQA groups of 4k heads) is a
-// function of the model's shapes alone, so a token's output has the same bits in
-// decode and in any chunked prefill, and an extra masked key is a no-op.
+// no second pass, and the route (the CUDA-core kernel here, the GQA kernel further down
+// -- q.k on the tensor cores, fold and P.V in fp32 -- for 16-bit data with D = 64 / 128
+// and GQA groups of 4k heads, or the generic kernel for other head dims) is a function
+// of the model's shapes alone, so a token's output has the same bits in decode and in
+// any chunked prefill, and an extra masked key is a no-op.
 //
 // B200 mapping:
 //   * K and V rows of the KV head are streamed through a ring of shared-memory
@@ -853,7 +854,7 @@ struct GqaPlan {
   static constexpr int XBUF = OVERLAP ? 2 : 1;
   static constexpr int COMB = GH * PARTIALS * D * 4 + 2 * GH * PARTIALS * 4 + 64;
   static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
-  static constexpr int SMEM = 1024 + REGION + XBUF * GH * XP * 4 + STAGES * 8 + 64;
+  static constexpr int SMEM = 1024 + REGION + XBUF * GH * XP * 4 + 2 * STAGES * 8 + 64;
   static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
   static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
 };
@@ -896,9 +897,13 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
   uint8_t* sK = smem;
   uint8_t* sV = smem + STAGES * TSB;
   float* xs = reinterpret_cast<float*>(smem + PL::REGION);  // scores [XBUF][GH][XP]
-  uint64_t* full = reinterpret_cast<uint64_t*>(xs + PL::XBUF * GH * XP);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + STAGES);
-  int* issued_count = const_cast<int*>(abort_flag) + 1;
+  // K and V of a stage complete on their own barriers, so a K slot refills as soon as
+  // its scores are out, while the fold and P.V of the stage still run
+  uint64_t* full_k = reinterpret_cast<uint64_t*>(xs + PL::XBUF * GH * XP);
+  uint64_t* full_v = full_k + STAGES;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full_v + STAGES);
+  int* issued_k = const_cast<int*>(abort_flag) + 1;
+  int* issued_v = issued_k + 1;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -962,14 +967,15 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
 #pragma unroll
       for (int i = 0; i < 4; ++i) o[h][c][i] = pack2(0.f, 0.f);
 
-  auto issue = [&](int blk) {
+  // one tensor's 128-key block into its ring slot (tid 0 only)
+  auto issue = [&](const CUtensorMap* map, uint8_t* ring, uint64_t* bars, int* issued, int blk) {
     const int st = blk % STAGES;
-    mbar_arrive_expect_tx(&full[st], 2 * TSB);
+    mbar_arrive_expect_tx(&bars[st], TSB);
 #pragma unroll
     for (int bx = 0; bx < D / BOX_D; ++bx) {
-      tma_load_4d(sK + st * TSB + bx * KEYS * 128, &tk, &full[st], bx * BOX_D, blk * KEYS, kvh, b);
-      tma_load_4d(sV + st * TSB + bx * KEYS * 128, &tv, &full[st], bx * BOX_D, blk * KEYS, kvh, b);
+      tma_load_4d(ring + st * TSB + bx * KEYS * 128, map, &bars[st], bx * BOX_D, blk * KEYS, kvh, b);
     }
+    *issued = blk + 1;
   };
   // A: scores of stage block t (its K in ring slot t % STAGES) into buffer xb.
   auto scores = [&](int t, float* xb) {
@@ -994,19 +1000,28 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
       xb[(2 * q4 + 1) * XP + k0 + 8] = c[3];
     }
   };
-  auto wait_stage = [&](int t) {
-    return mbar_wait(&full[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
+  // Every thread waits; the result is made warp-uniform, since the MMAs, ldmatrix and
+  // shuffles that follow need the whole warp.
+  auto wait_on = [&](uint64_t* bars, int t) {
+    const bool w = mbar_wait(&bars[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), abort_flag);
+    return __all_sync(0xffffffffu, w) != 0;
   };
 
   if (tid == 0) {
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    for (int st = 0; st < STAGES; ++st) mbar_init(&full[st], 1);
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full_k[st], 1);
+      mbar_init(&full_v[st], 1);
+    }
     *abort_flag = 0;
+    *issued_k = 0;
+    *issued_v = 0;
     fence_barrier_init();
-    int n0 = 0;
-    for (; n0 < STAGES && n0 < nblocks; ++n0) issue(n0);
-    *issued_count = n0;
+    for (int n0 = 0; n0 < STAGES && n0 < nblocks; ++n0) {
+      issue(&tk, sK, full_k, issued_k, n0);
+      issue(&tv, sV, full_v, issued_v, n0);
+    }
   }
   __syncthreads();
 
@@ -1015,7 +1030,7 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
   bool ok = true;
   if constexpr (OVERLAP) {
     if (nblocks > 0) {
-      ok = wait_stage(0);
+      ok = wait_on(full_k, 0);
       if (ok) scores(0, xs);
     }
   }
@@ -1023,7 +1038,7 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
     const int st = t % STAGES;
     float* xb = xs + (OVERLAP ? (t & 1) * GH * XP : 0);
     if constexpr (!OVERLAP) {
-      ok = wait_stage(t);
+      ok = wait_on(full_k, t);
       if (ok) scores(t, xb);
     }
     if (__syncthreads_or(!ok)) {
@@ -1034,13 +1049,12 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
       aborted = true;
       break;
     }
-    if constexpr (OVERLAP) {
-      // every warp is done with block t - 1 (its C) and with this block's A: refill
-      if (tid == 0 && t >= 1 && t - 1 + STAGES < nblocks) {
-        fence_proxy_async_smem();
-        issue(t - 1 + STAGES);
-        *issued_count = t - 1 + STAGES + 1;
-      }
+    // every warp is done with this block's A (its K slot is free) and, with OVERLAP,
+    // with block t - 1's C (its V slot is free)
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      if (t + STAGES < nblocks) issue(&tk, sK, full_k, issued_k, t + STAGES);
+      if (OVERLAP && t >= 1 && t - 1 + STAGES < nblocks) issue(&tv, sV, full_v, issued_v, t - 1 + STAGES);
     }
     const int64_t key0 = static_cast<int64_t>(t) * KEYS;
 
@@ -1094,7 +1108,9 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
     }
 
     // ---- C: o = o * f, then o = fmaf(e_j, v_j, o) for the visible keys, j ascending
+    const bool ok_v = wait_on(full_v, t);
     const uint32_t vbase = smem_u32(sV + st * TSB);
+    if (ok_v) {
 #pragma unroll
     for (int h = 0; h < GH; ++h) {
       const float fh = __shfl_sync(0xffffffffu, f, grp + TPH * h);
@@ -1133,26 +1149,47 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
         }
       }
     }
+    }  // ok_v
 
     if constexpr (OVERLAP) {
+      ok = ok_v;
       if (t + 1 < nblocks) {
-        ok = wait_stage(t + 1);
-        if (ok) scores(t + 1, xs + ((t + 1) & 1) * GH * XP);
+        const bool ok_k = wait_on(full_k, t + 1);
+        if (ok_k) scores(t + 1, xs + ((t + 1) & 1) * GH * XP);
+        ok = ok && ok_k;
       }
     } else {
-      __syncthreads();  // stage st and the scores are free
-      if (tid == 0 && t + STAGES < nblocks && !*abort_flag) {
+      if (__syncthreads_or(!ok_v)) {  // stage st's V and the scores are free
+        if (tid == 0) {
+          *abort_flag = 1;
+          record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
+        }
+        aborted = true;
+        break;
+      }
+      if (tid == 0 && t + STAGES < nblocks) {
         fence_proxy_async_smem();
-        issue(t + STAGES);
-        *issued_count = t + STAGES + 1;
+        issue(&tv, sV, full_v, issued_v, t + STAGES);
       }
     }
   }
+  // with OVERLAP the last stage's V wait is checked here
+  if (!aborted && __syncthreads_or(!ok)) {
+    if (tid == 0) {
+      *abort_flag = 1;
+      record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
+    }
+    aborted = true;
+  }
   if (aborted) {
     if (tid == 0) {
-      const int issued = *issued_count;
-      for (int blk = issued - STAGES < 0 ? 0 : issued - STAGES; blk < issued; ++blk) {
-        mbar_wait(&full[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
+      // wait, bounded, for every copy still in flight before the CTA leaves
+      const int ik = *issued_k, iv = *issued_v;
+      for (int blk = ik - STAGES < 0 ? 0 : ik - STAGES; blk < ik; ++blk) {
+        mbar_wait(&full_k[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
+      }
+      for (int blk = iv - STAGES < 0 ? 0 : iv - STAGES; blk < iv; ++blk) {
+        mbar_wait(&full_v[blk % STAGES], static_cast<uint32_t>((blk / STAGES) & 1), nullptr);
       }
     }
     return;
