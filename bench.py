@@ -28,7 +28,10 @@ Also reported:
 --profile gemm|gemm-decode|sdpa runs 3 warm-up launches and 1 launch of one kernel (the
 bench's dominant GEMM, config 5's M = 1 GEMM on (28672, 8192), or the bench's decode
 attention) and prints nothing (the target of the committed ncu captures).
---sweep prints config 5's table: bi.linear vs cuBLAS at M in 1..16384 on every shape.
+--sweep prints config 5's table: bi.linear vs cuBLAS at M in 1..16384 on every shape;
+under torchrun (--gpus N > 1) the column-parallel form on N GPUs -- the fused GEMM +
+NVLink all-gather against cuBLAS on the shard + NCCL all-gather -- timed as the max
+over ranks.
 """
 
 import argparse
@@ -331,17 +334,18 @@ def run_ours(args):
         if world > 1 else None
 
     def step(dom_events=None):
+        # dom_events: one (start, end) event pair per shape, recorded around its call
         outs = []
         for i, (K, N) in enumerate(SHAPES):
-            if dom_events is not None and i == DOMINANT:
-                dom_events[0].record()
+            if dom_events is not None:
+                dom_events[i][0].record()
             if world > 1:
                 # the copy of the peers' blocks runs on a side stream, under the next GEMM
                 y = fused[i].linear(xs[K], ws[i], out=ys[i], wait=False)
             else:
                 y = bi.linear(xs[K], ws[i])
-            if dom_events is not None and i == DOMINANT:
-                dom_events[1].record()
+            if dom_events is not None:
+                dom_events[i][1].record()
             outs.append(y)
         if world > 1:
             for f in fused:
@@ -364,8 +368,8 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    dom = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in SHAPES] for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _barrier_sync(world)
     e0.record()
@@ -397,7 +401,12 @@ def run_ours(args):
 
     # dominant kernel alone (its own events on its stream), same as in the step
     K, N = SHAPES[DOMINANT]
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom)
+    dom_ms = statistics.mean(ev[DOMINANT][0].elapsed_time(ev[DOMINANT][1]) for ev in dom)
+    # every call's mean device time, max over ranks (at N > 1 a call spans its entry
+    # barrier, the GEMM with its peer stores and the exit barrier)
+    per_call_us = [_max_over_ranks(statistics.mean(ev[i][0].elapsed_time(ev[i][1])
+                                                   for ev in dom) * 1e3, world)
+                   for i in range(len(SHAPES))]
     n_local = ws[DOMINANT].shape[0]
     dom_flops = 2.0 * M * K * n_local
     peaks, peak_src = _peaks()
@@ -565,6 +574,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline,
+        "per_call_us": per_call_us,
         "stock_cublas_tflops": cublas_tflops,
         "nccl_allgather_tflops": nccl_value,
         "fused_vs_single_gpu": bits_check,
@@ -707,6 +717,64 @@ def run_profile(args):
 SWEEP_M = (1, 8, 64, 512, 4096, 16384)
 
 
+def run_sweep_parallel(args):
+    """Config 5's sweep on N GPUs, column-parallel: every rank holds N/world rows of
+    each (N, K) weight and ends with the full (M, N) output.  Ours: FusedColumnParallel
+    (GEMM with the all-gather fused into the epilogue, the unpack included); stock:
+    cuBLAS on the shard, then an NCCL all-gather of the column blocks into (M, N)
+    (parallel.gather_columns).  Device time per call (CUDA events), max over ranks;
+    one markdown table from rank 0."""
+    from mlx_batch_invariant_b200 import parallel
+    world, rank, local = _dist_init(args)
+    dev = torch.device("cuda", local)
+    peaks, src = _peaks()
+    peak = peaks["bf16_tflops"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        _barrier_sync(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        _barrier_sync(world)
+        return _max_over_ranks(e0.elapsed_time(e1) / reps / 1e3, world)
+
+    if rank == 0:
+        print("| K | N | M | GPUs | fused µs | TFLOP/s (all GPUs) | of %d× tensor peak | "
+              "cuBLAS + NCCL µs | fused / stock |" % world)
+        print("|---|---|---|---|---|---|---|---|---|")
+    for K, N in SHAPES:
+        s0, s1 = parallel.shard_bounds(N, world)[rank]
+        w = (torch.randn((s1 - s0, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        fused = parallel.FusedColumnParallel(N, max(SWEEP_M), torch.bfloat16)
+        for Mr in SWEEP_M:
+            x = torch.randn((Mr, K), generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty((Mr, N), dtype=torch.bfloat16, device=dev)
+            reps = 20 if Mr < 4096 else 5
+            t_f = timed(lambda: fused.linear(x, w, out=y), reps)
+            t_s = timed(lambda: parallel.gather_columns(torch.nn.functional.linear(x, w), N), reps)
+            flops = 2.0 * Mr * N * K
+            if rank == 0:
+                print("| %d | %d | %d | %d | %.1f | %.1f | %.1f %% | %.1f | %.2f |"
+                      % (K, N, Mr, world, t_f * 1e6, flops / t_f / 1e12,
+                         100 * flops / t_f / 1e12 / (world * peak), t_s * 1e6, t_s / t_f),
+                      flush=True)
+            del x, y
+        fused.close()
+        del w
+    if rank == 0:
+        print("\npeaks: %s (bf16 %.0f TFLOP/s burst per GPU); fused / stock > 1 means the "
+              "fused path is faster" % (src, peak))
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_sweep(args):
     """Config 5's sweep on one GPU: bi.linear and stock F.linear (cuBLAS) at every
     (K, N) of SHAPES and M in SWEEP_M, bf16; one markdown table on stdout.  Every
@@ -761,12 +829,13 @@ def main(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile", choices=["gemm", "gemm-decode", "sdpa"], default=None)
     p.add_argument("--sweep", action="store_true",
-                   help="config 5's M sweep on one GPU (a markdown table, no JSON line)")
+                   help="config 5's M sweep (a markdown table, no JSON line); "
+                        "column-parallel under torchrun with --gpus N > 1")
     args = p.parse_args(argv)
     if args.profile:
         return run_profile(args)
     if args.sweep:
-        return run_sweep(args)
+        return run_sweep_parallel(args) if args.gpus > 1 else run_sweep(args)
     if args.warmup < 3:
         raise SystemExit("--warmup must be at least 3")
     if args.impl == "reference":

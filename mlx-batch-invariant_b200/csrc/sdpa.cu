@@ -835,26 +835,22 @@ __device__ __forceinline__ uint32_t kv_addr(uint32_t base, int row, int d) {
 //   C. numerator: o = o * f (skipped when f == 1), then o = fmaf(e_j, v_j, o) for the
 //      visible keys j = 0..3 in order, in fp32 (packed fma.rn.f32x2): the weights
 //      enter exactly.  Each V row is read once for the 4 heads.
-// With OVERLAP (a ring of two or more stages), A of stage t + 1 runs right after C of
-// stage t (scores double-buffered), so one CTA-wide barrier per stage remains.  A row's
-// arithmetic depends on its own q row, the keys and the mask only: an MMA column is
-// one head whatever the others hold, and every other step is per (head, partial).  GH,
-// the ring depth and OVERLAP decide which CTA, thread, buffer and barrier run a step,
-// never the step.
-template <int D, int GH_, int S_, bool OVERLAP_>
+// K and V of a stage complete on separate barriers: a K slot refills as soon as the
+// stage's scores are out, while its fold and P.V still run.  A row's arithmetic depends
+// on its own q row, the keys and the mask only: an MMA column is one head whatever the
+// others hold, and every other step is per (head, partial).  GH and the ring depth
+// decide which CTA, thread and buffer run a step, never the step.
+template <int D, int GH_, int S_>
 struct GqaPlan {
   static constexpr int GH = GH_;
   static constexpr int NT = 256;
   static constexpr int NCH = D / 64;        // 16-byte V vectors per thread per key
   static constexpr int TSB = KEYS * D * 2;  // one tensor's stage bytes
   static constexpr int STAGES = S_;
-  static constexpr bool OVERLAP = OVERLAP_;
-  static_assert(!OVERLAP_ || S_ >= 2, "overlap needs a second stage");
   static constexpr int XP = KEYS + 8;       // score row pitch (distinct banks for phase B)
-  static constexpr int XBUF = OVERLAP ? 2 : 1;
   static constexpr int COMB = GH * PARTIALS * D * 4 + 2 * GH * PARTIALS * 4 + 64;
   static constexpr int REGION = 2 * STAGES * TSB > COMB ? 2 * STAGES * TSB : COMB;
-  static constexpr int SMEM = 1024 + REGION + XBUF * GH * XP * 4 + 2 * STAGES * 8 + 64;
+  static constexpr int SMEM = 1024 + REGION + GH * XP * 4 + 2 * STAGES * 8 + 64;
   static constexpr int CTAS_PER_SM = 2 * SMEM <= 227 * 1024 ? 2 : 1;
   static_assert(SMEM <= 227 * 1024, "the stage ring must fit");
 };
@@ -876,11 +872,11 @@ __device__ __forceinline__ void widen8(const uint4 x, f2 (&v)[4]) {
 
 constexpr uint32_t kHiddenKey = 0x80000000u;  // -0.0f: the weight of a key not visible
 
-template <typename T, int D, int GH_, int S, bool OV>
-__global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
+template <typename T, int D, int GH_, int S>
+__global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S>::CTAS_PER_SM))
     sdpa_gqa_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const Params p) {
-  using PL = GqaPlan<D, GH_, S, OV>;
+  using PL = GqaPlan<D, GH_, S>;
   constexpr int GH = PL::GH;
   constexpr int NT = PL::NT;
   constexpr int NCH = PL::NCH;
@@ -888,7 +884,6 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
   constexpr int STAGES = PL::STAGES;
   constexpr int TSB = PL::TSB;
   constexpr int XP = PL::XP;
-  constexpr bool OVERLAP = PL::OVERLAP;
   static_assert(NT / 32 * 16 == KEYS, "one 16-key MMA tile per warp");
 
   extern __shared__ uint8_t smem_raw[];
@@ -896,10 +891,10 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + STAGES * TSB;
-  float* xs = reinterpret_cast<float*>(smem + PL::REGION);  // scores [XBUF][GH][XP]
+  float* xs = reinterpret_cast<float*>(smem + PL::REGION);  // scores [GH][XP]
   // K and V of a stage complete on their own barriers, so a K slot refills as soon as
   // its scores are out, while the fold and P.V of the stage still run
-  uint64_t* full_k = reinterpret_cast<uint64_t*>(xs + PL::XBUF * GH * XP);
+  uint64_t* full_k = reinterpret_cast<uint64_t*>(xs + GH * XP);
   uint64_t* full_v = full_k + STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full_v + STAGES);
   int* issued_k = const_cast<int*>(abort_flag) + 1;
@@ -1027,20 +1022,11 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
 
   const float scale = p.scale;
   bool aborted = false;
-  bool ok = true;
-  if constexpr (OVERLAP) {
-    if (nblocks > 0) {
-      ok = wait_on(full_k, 0);
-      if (ok) scores(0, xs);
-    }
-  }
   for (int t = 0; t < nblocks; ++t) {
     const int st = t % STAGES;
-    float* xb = xs + (OVERLAP ? (t & 1) * GH * XP : 0);
-    if constexpr (!OVERLAP) {
-      ok = wait_on(full_k, t);
-      if (ok) scores(t, xb);
-    }
+    float* xb = xs;
+    const bool ok = wait_on(full_k, t);
+    if (ok) scores(t, xb);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) {
         *abort_flag = 1;
@@ -1049,12 +1035,10 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
       aborted = true;
       break;
     }
-    // every warp is done with this block's A (its K slot is free) and, with OVERLAP,
-    // with block t - 1's C (its V slot is free)
-    if (tid == 0) {
+    // every warp is done with this block's A: its K slot is free
+    if (tid == 0 && t + STAGES < nblocks) {
       fence_proxy_async_smem();
-      if (t + STAGES < nblocks) issue(&tk, sK, full_k, issued_k, t + STAGES);
-      if (OVERLAP && t >= 1 && t - 1 + STAGES < nblocks) issue(&tv, sV, full_v, issued_v, t - 1 + STAGES);
+      issue(&tk, sK, full_k, issued_k, t + STAGES);
     }
     const int64_t key0 = static_cast<int64_t>(t) * KEYS;
 
@@ -1151,35 +1135,18 @@ __global__ void __launch_bounds__(256, (GqaPlan<D, GH_, S, OV>::CTAS_PER_SM))
     }
     }  // ok_v
 
-    if constexpr (OVERLAP) {
-      ok = ok_v;
-      if (t + 1 < nblocks) {
-        const bool ok_k = wait_on(full_k, t + 1);
-        if (ok_k) scores(t + 1, xs + ((t + 1) & 1) * GH * XP);
-        ok = ok && ok_k;
+    if (__syncthreads_or(!ok_v)) {  // stage st's V and the scores are free
+      if (tid == 0) {
+        *abort_flag = 1;
+        record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
       }
-    } else {
-      if (__syncthreads_or(!ok_v)) {  // stage st's V and the scores are free
-        if (tid == 0) {
-          *abort_flag = 1;
-          record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
-        }
-        aborted = true;
-        break;
-      }
-      if (tid == 0 && t + STAGES < nblocks) {
-        fence_proxy_async_smem();
-        issue(&tv, sV, full_v, issued_v, t + STAGES);
-      }
+      aborted = true;
+      break;
     }
-  }
-  // with OVERLAP the last stage's V wait is checked here
-  if (!aborted && __syncthreads_or(!ok)) {
-    if (tid == 0) {
-      *abort_flag = 1;
-      record_error(&g_error_word, (2u << 8) | kErrReasonTimeout);
+    if (tid == 0 && t + STAGES < nblocks) {
+      fence_proxy_async_smem();
+      issue(&tv, sV, full_v, issued_v, t + STAGES);
     }
-    aborted = true;
   }
   if (aborted) {
     if (tid == 0) {
@@ -1352,15 +1319,15 @@ static int kv_map(CUtensorMap* map, const void* base, const int64_t (&st)[2], co
   return encode_tiled16(map, base, 4, dims, strides, box, a.dtype);
 }
 
-template <typename T, int D, int GH, int S, bool OV>
+template <typename T, int D, int GH, int S>
 static int launch_gqa(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
-  using PL = GqaPlan<D, GH, S, OV>;
+  using PL = GqaPlan<D, GH, S>;
   CUtensorMap tk, tv;
   int st = kv_map<D>(&tk, a.k, a.ks, a);
   if (st) return st;
   st = kv_map<D>(&tv, a.v, a.vs, a);
   if (st) return st;
-  auto kern = sdpa_gqa_kernel<T, D, GH, S, OV>;
+  auto kern = sdpa_gqa_kernel<T, D, GH, S>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        PL::SMEM);
   if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sdpa gqa)");
@@ -1373,17 +1340,17 @@ static int launch_gqa(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
 // Heads per CTA and ring depth: GH = 4 shares each K/V stage between four heads; a grid
 // with few CTAs takes GH = 2 or 1 (the next GH while twice the CTAs still fit on the
 // SMs), which puts more SMs on the same keys (a KV head's stages then arrive once per
-// CTA, mostly from L2).  D = 128: a grid with more CTAs than SMs runs two 1-stage CTAs
-// per SM (each covers the other's load latency), a smaller one a 3-stage ring per SM;
-// D = 64: always the 3-stage ring with A of the next stage overlapping, two CTAs per
-// SM.  Measured on B200 (decode, L = 8192): GH = 2 with two 1-stage CTAs per SM for a
-// 512-row grid ran 160 us against 139 us for GH = 4 with one 3-stage CTA per SM; the
-// overlap gained at D = 64 (229 vs 232 us) and not at D = 128.  None of these changes a
-// row's bits.
+// CTA, mostly from L2).  A grid with more CTAs than SMs runs two 1-stage CTAs per SM
+// (each covers the other's load latency), a smaller one a 3-stage ring per SM.
+// Measured on B200 (decode, L = 8192): GH = 2 with two 1-stage CTAs per SM for a
+// 512-row grid ran 160 us against 139 us for GH = 4 with one 3-stage CTA per SM; at
+// D = 64 this plan beat two 3-stage CTAs per SM (235 vs 234-249 us at B = 64, H = 32;
+// 71 vs 82-86 us at H = 4), and overlapping the next stage's scores with P.V gained
+// nothing once K and V had separate barriers.  None of these changes a row's bits.
 template <typename T, int D, int GH>
 static int launch_gh(const SdpaArgs& a, const Params& p, cudaStream_t stream, bool big) {
-  if (big) return launch_gqa<T, D, GH, 1, false>(a, p, stream);
-  return launch_gqa<T, D, GH, 3, D == 64>(a, p, stream);
+  if (big) return launch_gqa<T, D, GH, 1>(a, p, stream);
+  return launch_gqa<T, D, GH, 3>(a, p, stream);
 }
 
 template <typename T, int D>
@@ -1392,11 +1359,7 @@ static int launch(const SdpaArgs& a, const Params& p, cudaStream_t stream) {
   const int64_t rows = a.B * a.H * a.qL;  // query (row, head) pairs
   int gh = 4;
   bool big;
-  if (D == 64) {
-    // 3-stage CTAs fit two per SM
-    while (gh > 1 && 2 * (rows / gh) <= 2 * sms) gh /= 2;
-    big = false;
-  } else if (rows / 4 > sms) {
+  if (rows / 4 > sms) {
     big = true;  // two 1-stage CTAs per SM
   } else {
     while (gh > 1 && 2 * (rows / gh) <= sms) gh /= 2;
