@@ -25,9 +25,10 @@ Also reported:
             the reference itself is Metal-only) on a bounded sample, rank 0, N = 1.
 
 --impl reference times that CPU implementation alone on the same metric (rank 0).
---profile gemm|gemm-decode|sdpa runs 3 warm-up launches and 1 launch of one kernel (the
-bench's dominant GEMM, config 5's M = 1 GEMM on (28672, 8192), or the bench's decode
-attention) and prints nothing (the target of the committed ncu captures).
+--profile gemm|gemm-decode|gemm-tf32x3|sdpa runs 3 warm-up launches and 1 launch of one
+kernel (the bench's dominant GEMM, config 5's M = 1 GEMM on (28672, 8192), the fp32
+tensor-core GEMM at M = 4096, K = N = 8192, or the bench's decode attention) and prints
+nothing (the target of the committed ncu captures).
 --sweep prints config 5's table: bi.linear vs cuBLAS at M in 1..16384 on every shape;
 under torchrun (--gpus N > 1) the column-parallel form on N GPUs -- the fused GEMM +
 NVLink all-gather against cuBLAS on the shard + NCCL all-gather -- timed as the max
@@ -702,6 +703,13 @@ def run_profile(args):
         w = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
         for _ in range(4):
             bi.linear(x, w)
+    elif args.profile == "gemm-tf32x3":
+        # float32 on the tensor cores (opt-in route): M = 4096, K = N = 8192
+        x = torch.randn((M, 8192), generator=g, device=dev)
+        w = torch.randn((8192, 8192), generator=g, device=dev) * 8192 ** -0.5
+        with bi.float32_gemm("tf32x3"):
+            for _ in range(4):
+                bi.linear(x, w)
     else:
         c = SDPA_CFG
         q = torch.randn((c["B"], c["H"], 1, c["D"]), generator=g, device=dev).to(torch.bfloat16)
@@ -827,7 +835,8 @@ def main(argv=None):
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--profile", choices=["gemm", "gemm-decode", "sdpa"], default=None)
+    p.add_argument("--profile", choices=["gemm", "gemm-decode", "gemm-tf32x3", "sdpa"],
+                   default=None)
     p.add_argument("--sweep", action="store_true",
                    help="config 5's M sweep (a markdown table, no JSON line); "
                         "column-parallel under torchrun with --gpus N > 1")
